@@ -1,0 +1,606 @@
+// api.cu - the C ABI of libgpullama_attn (include/gpullama_attn.h).
+//
+// Argument checking, the context (device, stream, workspace, status word,
+// communicator) and dispatch to the kernel launchers.  Every entry point
+// returns a status code; no exception crosses the ABI.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <exception>
+#include <string>
+#include <vector>
+
+#include "../../include/gpullama_attn.h"
+#include "gla_common.cuh"
+#include "gla_internal.h"
+#include "gla_comm.h"
+
+struct gla_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  gla::DeviceInfo dev{};
+  int32_t* status = nullptr;        // device status word
+  int32_t* counters = nullptr;      // piece counters (zero between calls)
+  size_t counters_cap = 0;
+  float* parts = nullptr;           // piece slots
+  size_t parts_cap = 0;             // floats
+  float* records = nullptr;         // sharded decode: local records
+  float* gathered = nullptr;        // sharded decode: all ranks' records
+  size_t records_cap = 0;           // floats per rank
+  gla::Comm comm;
+  std::string last_error;
+};
+
+namespace {
+
+int fail(gla_ctx* ctx, int code, const std::string& msg) {
+  if (ctx) ctx->last_error = msg;
+  return code;
+}
+
+int cuda_fail(gla_ctx* ctx, cudaError_t e, const char* what) {
+  return fail(ctx, GLA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Makes the context's device current for the duration of a call.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = true;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+bool stream_capturing(cudaStream_t s) {
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &st) != cudaSuccess) return false;
+  return st != cudaStreamCaptureStatusNone;
+}
+
+// Grows the piece workspace; never during stream capture.
+int ensure_workspace(gla_ctx* ctx, size_t part_floats, size_t counters) {
+  if (part_floats <= ctx->parts_cap && counters <= ctx->counters_cap) return GLA_OK;
+  if (stream_capturing(ctx->stream))
+    return fail(ctx, GLA_ERR_INVALID_ARG,
+                "decode workspace must grow; call gla_reserve before stream capture");
+  cudaError_t e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamSynchronize");
+  if (part_floats > ctx->parts_cap) {
+    size_t cap = std::max(part_floats, ctx->parts_cap * 2);
+    cudaFree(ctx->parts);
+    ctx->parts = nullptr;
+    ctx->parts_cap = 0;
+    e = cudaMalloc(&ctx->parts, cap * sizeof(float));
+    if (e != cudaSuccess) return fail(ctx, GLA_ERR_OUT_OF_MEMORY, "workspace allocation failed");
+    ctx->parts_cap = cap;
+  }
+  if (counters > ctx->counters_cap) {
+    size_t cap = std::max(counters, ctx->counters_cap * 2);
+    cudaFree(ctx->counters);
+    ctx->counters = nullptr;
+    ctx->counters_cap = 0;
+    e = cudaMalloc(&ctx->counters, cap * sizeof(int32_t));
+    if (e != cudaSuccess) return fail(ctx, GLA_ERR_OUT_OF_MEMORY, "workspace allocation failed");
+    e = cudaMemsetAsync(ctx->counters, 0, cap * sizeof(int32_t), ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemsetAsync");
+    ctx->counters_cap = cap;
+  }
+  return GLA_OK;
+}
+
+int check_decode_shape(gla_ctx* ctx, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                       int64_t kv_stride, int esize) {
+  if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "n_heads, n_kv_heads and head_dim must be positive");
+  if (n_heads % n_kv_heads != 0)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "n_heads must be a multiple of n_kv_heads");
+  if (kv_stride < (int64_t)n_kv_heads * head_dim)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "kv_stride must be >= n_kv_heads * head_dim");
+  if ((kv_stride * esize) % 16 != 0 || ((int64_t)head_dim * esize) % 16 != 0)
+    return fail(ctx, GLA_ERR_ALIGNMENT, "kv_stride and head_dim must be multiples of 16 bytes");
+  return GLA_OK;
+}
+
+int run_decode(gla_ctx* ctx, gla::DecodeRequest& req) {
+  std::string err;
+  gla::DecodePlan plan;
+  int rc = gla::plan_decode(req, ctx->dev, &plan, &err);
+  if (rc != GLA_OK) return fail(ctx, rc, err);
+  rc = ensure_workspace(ctx, plan.part_floats, plan.counters);
+  if (rc != GLA_OK) return rc;
+  rc = gla::launch_decode(req, plan, ctx->parts, ctx->counters, ctx->status, ctx->stream, &err);
+  if (rc != GLA_OK) return fail(ctx, rc, err);
+  return GLA_OK;
+}
+
+int decode_single(gla_ctx* ctx, int dtype, const float* q, const void* k, const void* v,
+                  float* out, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                  int64_t kv_stride, int32_t n_pos, float scale, int32_t record_mode) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  if (!q || !k || !v || !out) return fail(ctx, GLA_ERR_INVALID_ARG, "null tensor pointer");
+  if (n_pos < 1) return fail(ctx, GLA_ERR_INVALID_ARG, "n_pos must be >= 1");
+  if (!std::isfinite(scale)) return fail(ctx, GLA_ERR_INVALID_ARG, "scale must be finite");
+  const int esize = dtype == GLA_DTYPE_F32 ? 4 : 2;
+  int rc = check_decode_shape(ctx, n_heads, n_kv_heads, head_dim, kv_stride, esize);
+  if (rc != GLA_OK) return rc;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return fail(ctx, GLA_ERR_ALIGNMENT, "q, k, v and the output must be 16-byte aligned");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, GLA_ERR_CUDA, "cudaSetDevice failed");
+  gla::DecodeRequest req{};
+  req.dtype = dtype;
+  req.q = q;
+  req.k = k;
+  req.v = v;
+  req.kv_stride = kv_stride;
+  req.n_pos = n_pos;
+  req.n_pos_cap = n_pos;
+  req.max_n_pos = n_pos;
+  req.batch = 1;
+  req.n_heads = n_heads;
+  req.n_kv = n_kv_heads;
+  req.head_dim = head_dim;
+  req.scale = scale;
+  req.out = out;
+  req.record_mode = record_mode;
+  return run_decode(ctx, req);
+}
+
+int decode_batched(gla_ctx* ctx, int dtype, const float* q, const void* const* k_ptrs,
+                   const void* const* v_ptrs, const int32_t* n_pos, int32_t max_n_pos,
+                   float* xb, int32_t batch, int32_t n_heads, int32_t n_kv_heads,
+                   int32_t head_dim, int64_t kv_stride, float scale) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  if (!q || !k_ptrs || !v_ptrs || !n_pos || !xb)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "null pointer");
+  if (batch < 1) return fail(ctx, GLA_ERR_INVALID_ARG, "batch must be >= 1");
+  if (max_n_pos < 1) return fail(ctx, GLA_ERR_INVALID_ARG, "max_n_pos must be >= 1");
+  if (!std::isfinite(scale)) return fail(ctx, GLA_ERR_INVALID_ARG, "scale must be finite");
+  const int esize = dtype == GLA_DTYPE_F32 ? 4 : 2;
+  int rc = check_decode_shape(ctx, n_heads, n_kv_heads, head_dim, kv_stride, esize);
+  if (rc != GLA_OK) return rc;
+  if (!aligned16(q) || !aligned16(xb))
+    return fail(ctx, GLA_ERR_ALIGNMENT, "q and xb must be 16-byte aligned");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, GLA_ERR_CUDA, "cudaSetDevice failed");
+  gla::DecodeRequest req{};
+  req.dtype = dtype;
+  req.q = q;
+  req.k_ptrs = k_ptrs;
+  req.v_ptrs = v_ptrs;
+  req.kv_stride = kv_stride;
+  req.n_pos_dev = n_pos;
+  req.n_pos_add = 0;
+  req.n_pos_cap = max_n_pos;
+  req.max_n_pos = max_n_pos;
+  req.batch = batch;
+  req.n_heads = n_heads;
+  req.n_kv = n_kv_heads;
+  req.head_dim = head_dim;
+  req.scale = scale;
+  req.out = xb;
+  req.record_mode = 0;
+  return run_decode(ctx, req);
+}
+
+int process_heads(gla_ctx* ctx, int dtype, const float* q, const void* key_cache,
+                  const void* value_cache, float* xb, int32_t n_heads, int32_t head_size,
+                  int32_t kv_dim, int32_t kv_mul, const int32_t* position_holder, int32_t layer,
+                  int32_t context_length) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  if (!q || !key_cache || !value_cache || !xb || !position_holder)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "null pointer");
+  if (kv_mul <= 0 || n_heads <= 0 || n_heads % kv_mul != 0)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "kvMul must divide nHeads");
+  const int32_t n_kv = n_heads / kv_mul;
+  if ((int64_t)n_kv * head_size != kv_dim)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "kvDim must equal (nHeads / kvMul) * headSize");
+  if (layer < 0 || context_length < 1)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "layer must be >= 0 and contextLength >= 1");
+  const int esize = dtype == GLA_DTYPE_F32 ? 4 : 2;
+  int rc = check_decode_shape(ctx, n_heads, n_kv, head_size, kv_dim, esize);
+  if (rc != GLA_OK) return rc;
+  if (!aligned16(q) || !aligned16(key_cache) || !aligned16(value_cache) || !aligned16(xb))
+    return fail(ctx, GLA_ERR_ALIGNMENT, "q, caches and xb must be 16-byte aligned");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, GLA_ERR_CUDA, "cudaSetDevice failed");
+  const int64_t loff = (int64_t)layer * context_length * kv_dim * esize;  // 64-bit layer offset
+  gla::DecodeRequest req{};
+  req.dtype = dtype;
+  req.q = q;
+  req.k = static_cast<const char*>(key_cache) + loff;
+  req.v = static_cast<const char*>(value_cache) + loff;
+  req.kv_stride = kv_dim;
+  req.n_pos_dev = position_holder;
+  req.n_pos_add = 1;
+  req.n_pos_cap = context_length;
+  req.max_n_pos = context_length;
+  req.batch = 1;
+  req.n_heads = n_heads;
+  req.n_kv = n_kv;
+  req.head_dim = head_size;
+  req.scale = (float)(1.0 / std::sqrt((double)head_size));
+  req.out = xb;
+  req.record_mode = 0;
+  return run_decode(ctx, req);
+}
+
+int sharded(gla_ctx* ctx, int dtype, const float* q, const void* k, const void* v, float* xb,
+            int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int64_t kv_stride,
+            int32_t n_pos_local, float scale) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  if (!ctx->comm.active())
+    return fail(ctx, GLA_ERR_COMM, "gla_comm_init has not been called on this context");
+  if (!xb) return fail(ctx, GLA_ERR_INVALID_ARG, "null xb");
+  const size_t rec = (size_t)n_heads * (head_dim + 2);
+  if (rec > ctx->records_cap) {
+    if (stream_capturing(ctx->stream))
+      return fail(ctx, GLA_ERR_INVALID_ARG, "record buffers must grow outside stream capture");
+    DeviceGuard dg(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(ctx->records);
+    cudaFree(ctx->gathered);
+    ctx->records = ctx->gathered = nullptr;
+    ctx->records_cap = 0;
+    if (cudaMalloc(&ctx->records, rec * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&ctx->gathered, rec * ctx->comm.nranks * sizeof(float)) != cudaSuccess)
+      return fail(ctx, GLA_ERR_OUT_OF_MEMORY, "record buffer allocation failed");
+    ctx->records_cap = rec;
+  }
+  int rc;
+  if (n_pos_local >= 1) {
+    rc = decode_single(ctx, dtype, q, k, v, ctx->records, n_heads, n_kv_heads, head_dim, kv_stride,
+                       n_pos_local, scale, 1);
+    if (rc != GLA_OK) return rc;
+  } else {
+    // an empty shard contributes l = 0 records
+    DeviceGuard dg(ctx->device);
+    cudaMemsetAsync(ctx->records, 0, rec * sizeof(float), ctx->stream);
+  }
+  DeviceGuard dg(ctx->device);
+  std::string err;
+  rc = ctx->comm.all_gather(ctx->records, ctx->gathered, rec, ctx->stream, &err);
+  if (rc != GLA_OK) return fail(ctx, rc, err);
+  rc = gla::launch_lse_combine(ctx->gathered, ctx->comm.nranks, n_heads, head_dim, xb,
+                               ctx->stream, &err);
+  if (rc != GLA_OK) return fail(ctx, rc, err);
+  return GLA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t gla_version(void) { return GLA_VERSION; }
+
+const char* gla_status_string(int32_t status) {
+  switch (status) {
+    case GLA_OK: return "GLA_OK";
+    case GLA_ERR_INVALID_ARG: return "GLA_ERR_INVALID_ARG";
+    case GLA_ERR_CUDA: return "GLA_ERR_CUDA";
+    case GLA_ERR_NOT_SUPPORTED: return "GLA_ERR_NOT_SUPPORTED";
+    case GLA_ERR_ALIGNMENT: return "GLA_ERR_ALIGNMENT";
+    case GLA_ERR_TIMEOUT: return "GLA_ERR_TIMEOUT";
+    case GLA_ERR_COMM: return "GLA_ERR_COMM";
+    case GLA_ERR_NO_DEVICE: return "GLA_ERR_NO_DEVICE";
+    case GLA_ERR_OUT_OF_MEMORY: return "GLA_ERR_OUT_OF_MEMORY";
+    default: return "GLA_ERR_UNKNOWN";
+  }
+}
+
+int32_t gla_create(int32_t device, void* cuda_stream, gla_ctx** out) {
+  if (!out) return GLA_ERR_INVALID_ARG;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return GLA_ERR_NO_DEVICE;
+  }
+  if (device < 0 || device >= n) return GLA_ERR_NO_DEVICE;
+  gla_ctx* ctx = nullptr;
+  try {
+    ctx = new gla_ctx();
+  } catch (const std::exception&) {
+    return GLA_ERR_OUT_OF_MEMORY;
+  }
+  ctx->device = device;
+  ctx->stream = static_cast<cudaStream_t>(cuda_stream);
+  DeviceGuard dg(device);
+  if (!dg.ok) {
+    delete ctx;
+    return GLA_ERR_CUDA;
+  }
+  cudaDeviceGetAttribute(&ctx->dev.sms, cudaDevAttrMultiProcessorCount, device);
+  cudaDeviceGetAttribute(&ctx->dev.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  if (cudaMalloc(&ctx->status, 256) != cudaSuccess) {
+    delete ctx;
+    return GLA_ERR_OUT_OF_MEMORY;
+  }
+  cudaMemset(ctx->status, 0, 256);
+  *out = ctx;
+  return GLA_OK;
+}
+
+int32_t gla_destroy(gla_ctx* ctx) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  {
+    DeviceGuard dg(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    ctx->comm.destroy();
+    cudaFree(ctx->status);
+    cudaFree(ctx->counters);
+    cudaFree(ctx->parts);
+    cudaFree(ctx->records);
+    cudaFree(ctx->gathered);
+  }
+  delete ctx;
+  return GLA_OK;
+}
+
+int32_t gla_set_stream(gla_ctx* ctx, void* cuda_stream) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  ctx->stream = static_cast<cudaStream_t>(cuda_stream);
+  return GLA_OK;
+}
+
+const char* gla_last_error(const gla_ctx* ctx) { return ctx ? ctx->last_error.c_str() : ""; }
+
+int32_t gla_device_status(gla_ctx* ctx, int32_t* device_status) {
+  if (!ctx || !device_status) return GLA_ERR_INVALID_ARG;
+  DeviceGuard dg(ctx->device);
+  cudaError_t e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamSynchronize");
+  int32_t v = 0;
+  e = cudaMemcpy(&v, ctx->status, sizeof v, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpy");
+  if (v != 0) {
+    cudaMemset(ctx->status, 0, sizeof v);
+    // a kernel that gave up may have left piece counters raised
+    if (ctx->counters) cudaMemset(ctx->counters, 0, ctx->counters_cap * sizeof(int32_t));
+  }
+  *device_status = v;
+  return GLA_OK;
+}
+
+int32_t gla_reserve(gla_ctx* ctx, int32_t max_batch, int32_t max_kv_heads, int32_t max_heads,
+                    int32_t max_head_dim) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  if (max_batch < 1 || max_kv_heads < 1 || max_heads < 1 || max_head_dim < 1)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "reserve sizes must be positive");
+  const int group = std::max(1, max_heads / max_kv_heads);
+  DeviceGuard dg(ctx->device);
+  const size_t part = (size_t)(ctx->dev.sms + (size_t)max_batch * max_kv_heads) * group *
+                      (max_head_dim + 2);
+  return ensure_workspace(ctx, part, (size_t)max_batch * max_kv_heads);
+}
+
+int32_t gla_num_sms(const gla_ctx* ctx) { return ctx ? ctx->dev.sms : 0; }
+
+int32_t gla_kv_cache_alloc(gla_ctx* ctx, int32_t n_layers, int32_t context_length, int32_t kv_dim,
+                           int32_t dtype, void** key_cache, void** value_cache) {
+  if (!ctx || !key_cache || !value_cache) return GLA_ERR_INVALID_ARG;
+  *key_cache = *value_cache = nullptr;
+  if (n_layers < 1 || context_length < 1 || kv_dim < 1)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "cache dimensions must be positive");
+  if (dtype != GLA_DTYPE_F32 && dtype != GLA_DTYPE_F16)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "dtype must be GLA_DTYPE_F32 or GLA_DTYPE_F16");
+  const size_t bytes =
+      (size_t)n_layers * context_length * kv_dim * (dtype == GLA_DTYPE_F32 ? 4 : 2);
+  DeviceGuard dg(ctx->device);
+  void* k = nullptr;
+  void* v = nullptr;
+  if (cudaMalloc(&k, bytes) != cudaSuccess || cudaMalloc(&v, bytes) != cudaSuccess) {
+    cudaFree(k);
+    cudaGetLastError();
+    return fail(ctx, GLA_ERR_OUT_OF_MEMORY, "KV cache allocation failed");
+  }
+  cudaMemsetAsync(k, 0, bytes, ctx->stream);
+  cudaMemsetAsync(v, 0, bytes, ctx->stream);
+  *key_cache = k;
+  *value_cache = v;
+  return GLA_OK;
+}
+
+int32_t gla_kv_cache_free(gla_ctx* ctx, void* key_cache, void* value_cache) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  DeviceGuard dg(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  cudaFree(key_cache);
+  cudaFree(value_cache);
+  return GLA_OK;
+}
+
+int32_t gla_process_heads_flash_attention(gla_ctx* ctx, const float* q, const float* key_cache,
+                                          const float* value_cache, float* xb, int32_t n_heads,
+                                          int32_t head_size, int32_t kv_dim, int32_t kv_mul,
+                                          const int32_t* position_holder, int32_t layer,
+                                          int32_t context_length) {
+  return process_heads(ctx, GLA_DTYPE_F32, q, key_cache, value_cache, xb, n_heads, head_size,
+                       kv_dim, kv_mul, position_holder, layer, context_length);
+}
+
+int32_t gla_process_heads_flash_attention_f16kv(gla_ctx* ctx, const float* q,
+                                                const uint16_t* key_cache,
+                                                const uint16_t* value_cache, float* xb,
+                                                int32_t n_heads, int32_t head_size, int32_t kv_dim,
+                                                int32_t kv_mul, const int32_t* position_holder,
+                                                int32_t layer, int32_t context_length) {
+  return process_heads(ctx, GLA_DTYPE_F16, q, key_cache, value_cache, xb, n_heads, head_size,
+                       kv_dim, kv_mul, position_holder, layer, context_length);
+}
+
+int32_t gla_decode_f32kv(gla_ctx* ctx, const float* q, const float* k, const float* v, float* xb,
+                         int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int64_t kv_stride,
+                         int32_t n_pos, float scale) {
+  return decode_single(ctx, GLA_DTYPE_F32, q, k, v, xb, n_heads, n_kv_heads, head_dim, kv_stride,
+                       n_pos, scale, 0);
+}
+
+int32_t gla_decode_f16kv(gla_ctx* ctx, const float* q, const uint16_t* k, const uint16_t* v,
+                         float* xb, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                         int64_t kv_stride, int32_t n_pos, float scale) {
+  return decode_single(ctx, GLA_DTYPE_F16, q, k, v, xb, n_heads, n_kv_heads, head_dim, kv_stride,
+                       n_pos, scale, 0);
+}
+
+int32_t gla_decode_batched_f32kv(gla_ctx* ctx, const float* q, const float* const* k_ptrs,
+                                 const float* const* v_ptrs, const int32_t* n_pos,
+                                 int32_t max_n_pos, float* xb, int32_t batch, int32_t n_heads,
+                                 int32_t n_kv_heads, int32_t head_dim, int64_t kv_stride,
+                                 float scale) {
+  return decode_batched(ctx, GLA_DTYPE_F32, q, reinterpret_cast<const void* const*>(k_ptrs),
+                        reinterpret_cast<const void* const*>(v_ptrs), n_pos, max_n_pos, xb, batch,
+                        n_heads, n_kv_heads, head_dim, kv_stride, scale);
+}
+
+int32_t gla_decode_batched_f16kv(gla_ctx* ctx, const float* q, const uint16_t* const* k_ptrs,
+                                 const uint16_t* const* v_ptrs, const int32_t* n_pos,
+                                 int32_t max_n_pos, float* xb, int32_t batch, int32_t n_heads,
+                                 int32_t n_kv_heads, int32_t head_dim, int64_t kv_stride,
+                                 float scale) {
+  return decode_batched(ctx, GLA_DTYPE_F16, q, reinterpret_cast<const void* const*>(k_ptrs),
+                        reinterpret_cast<const void* const*>(v_ptrs), n_pos, max_n_pos, xb, batch,
+                        n_heads, n_kv_heads, head_dim, kv_stride, scale);
+}
+
+int32_t gla_decode_partial_f32kv(gla_ctx* ctx, const float* q, const float* k, const float* v,
+                                 float* part, int32_t n_heads, int32_t n_kv_heads,
+                                 int32_t head_dim, int64_t kv_stride, int32_t n_pos, float scale) {
+  return decode_single(ctx, GLA_DTYPE_F32, q, k, v, part, n_heads, n_kv_heads, head_dim,
+                       kv_stride, n_pos, scale, 1);
+}
+
+int32_t gla_decode_partial_f16kv(gla_ctx* ctx, const float* q, const uint16_t* k,
+                                 const uint16_t* v, float* part, int32_t n_heads,
+                                 int32_t n_kv_heads, int32_t head_dim, int64_t kv_stride,
+                                 int32_t n_pos, float scale) {
+  return decode_single(ctx, GLA_DTYPE_F16, q, k, v, part, n_heads, n_kv_heads, head_dim,
+                       kv_stride, n_pos, scale, 1);
+}
+
+int32_t gla_lse_combine(gla_ctx* ctx, const float* parts, int32_t n_parts, int32_t n_heads,
+                        int32_t head_dim, float* xb) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  if (!parts || !xb) return fail(ctx, GLA_ERR_INVALID_ARG, "null pointer");
+  if (n_parts < 1 || n_heads < 1 || head_dim < 1)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "n_parts, n_heads and head_dim must be positive");
+  DeviceGuard dg(ctx->device);
+  std::string err;
+  int rc = gla::launch_lse_combine(parts, n_parts, n_heads, head_dim, xb, ctx->stream, &err);
+  return rc == GLA_OK ? GLA_OK : fail(ctx, rc, err);
+}
+
+int32_t gla_comm_unique_id_size(void) { return gla::Comm::unique_id_size(); }
+
+int32_t gla_comm_get_unique_id(void* unique_id) {
+  if (!unique_id) return GLA_ERR_INVALID_ARG;
+  std::string err;
+  return gla::Comm::get_unique_id(unique_id, &err);
+}
+
+int32_t gla_comm_init(gla_ctx* ctx, int32_t nranks, int32_t rank, const void* unique_id) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  if (!unique_id || nranks < 1 || rank < 0 || rank >= nranks)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "bad communicator arguments");
+  DeviceGuard dg(ctx->device);
+  std::string err;
+  int rc = ctx->comm.init(nranks, rank, unique_id, &err);
+  return rc == GLA_OK ? GLA_OK : fail(ctx, rc, err);
+}
+
+int32_t gla_decode_sharded_f16kv(gla_ctx* ctx, const float* q, const uint16_t* k,
+                                 const uint16_t* v, float* xb, int32_t n_heads,
+                                 int32_t n_kv_heads, int32_t head_dim, int64_t kv_stride,
+                                 int32_t n_pos_local, float scale) {
+  return sharded(ctx, GLA_DTYPE_F16, q, k, v, xb, n_heads, n_kv_heads, head_dim, kv_stride,
+                 n_pos_local, scale);
+}
+
+int32_t gla_decode_sharded_f32kv(gla_ctx* ctx, const float* q, const float* k, const float* v,
+                                 float* xb, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                 int64_t kv_stride, int32_t n_pos_local, float scale) {
+  return sharded(ctx, GLA_DTYPE_F32, q, k, v, xb, n_heads, n_kv_heads, head_dim, kv_stride,
+                 n_pos_local, scale);
+}
+
+int32_t gla_prefill_causal_f16(gla_ctx* ctx, const uint16_t* q, const uint16_t* k,
+                               const uint16_t* v, float* out, int32_t L, int32_t n_heads,
+                               int32_t n_kv_heads, int32_t head_dim, float scale) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  if (!q || !k || !v || !out) return fail(ctx, GLA_ERR_INVALID_ARG, "null tensor pointer");
+  if (L < 1 || n_heads < 1 || n_kv_heads < 1 || n_heads % n_kv_heads != 0)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "bad prefill shape");
+  if (!std::isfinite(scale)) return fail(ctx, GLA_ERR_INVALID_ARG, "scale must be finite");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return fail(ctx, GLA_ERR_ALIGNMENT, "prefill tensors must be 16-byte aligned");
+  DeviceGuard dg(ctx->device);
+  std::string err;
+  int rc = gla::launch_prefill_f16(q, k, v, out, L, n_heads, n_kv_heads, head_dim, scale,
+                                   ctx->status, ctx->dev, ctx->stream, &err);
+  return rc == GLA_OK ? GLA_OK : fail(ctx, rc, err);
+}
+
+int32_t gla_rope_append_f32(gla_ctx* ctx, float* q, float* k, const float* v, float* key_cache,
+                            float* value_cache, int32_t n_heads, int32_t n_kv_heads,
+                            int32_t head_dim, const int32_t* position_holder, float theta,
+                            int32_t rope_style) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  if (!q || !k || !v || !key_cache || !value_cache || !position_holder)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "null pointer");
+  if (n_heads < 1 || n_kv_heads < 1 || n_kv_heads > n_heads || head_dim < 2 || head_dim % 2)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "bad RoPE shape");
+  if (rope_style != GLA_ROPE_INTERLEAVED && rope_style != GLA_ROPE_NEOX)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "unknown rope_style");
+  if (!(theta > 0.f)) return fail(ctx, GLA_ERR_INVALID_ARG, "theta must be positive");
+  DeviceGuard dg(ctx->device);
+  std::string err;
+  int rc = gla::launch_rope_append_f32(q, k, v, key_cache, value_cache, n_heads, n_kv_heads,
+                                       head_dim, position_holder, theta, rope_style, ctx->stream,
+                                       &err);
+  return rc == GLA_OK ? GLA_OK : fail(ctx, rc, err);
+}
+
+int64_t gla_debug_partition(const int32_t* n_pos, int32_t n_seq, int32_t n_kv_heads, int32_t tile,
+                            int32_t n_ctas, int32_t* cta, int32_t* seq, int32_t* kv_head,
+                            int32_t* row0, int32_t* slot, int64_t capacity) {
+  if (!n_pos || n_seq < 1 || n_kv_heads < 1 || tile < 1 || n_ctas < 1)
+    return GLA_ERR_INVALID_ARG;
+  std::vector<int32_t> ntiles(n_seq), start(n_seq + 1);
+  int64_t acc = 0;
+  for (int b = 0; b < n_seq; ++b) {
+    int32_t np = n_pos[b] < 0 ? 0 : n_pos[b];
+    ntiles[b] = gla::ceil_div(np, tile);
+    start[b] = (int32_t)(acc * n_kv_heads);
+    acc += ntiles[b];
+  }
+  start[n_seq] = (int32_t)(acc * n_kv_heads);
+  const int32_t W = start[n_seq];
+  if (W > capacity) return GLA_ERR_INVALID_ARG;
+  const gla::Split sp = gla::make_split(W, n_ctas);
+  // walk each CTA's range exactly as the kernel's producer/consumers do
+  for (int32_t c = 0; c < n_ctas; ++c) {
+    const int32_t lo = gla::split_lo(sp, c), cnt = gla::split_count(sp, c);
+    if (cnt == 0) continue;
+    gla::TileRef tr = gla::locate_tile(start.data(), ntiles.data(), n_seq, n_kv_heads, lo);
+    for (int32_t i = 0; i < cnt; ++i) {
+      const int32_t t = lo + i;
+      cta[t] = c;
+      seq[t] = tr.b;
+      kv_head[t] = tr.g;
+      row0[t] = tr.j * tile;
+      slot[t] = c + tr.b * n_kv_heads + tr.g;
+      gla::next_tile(tr, ntiles.data(), n_seq, n_kv_heads);
+    }
+  }
+  return W;
+}
+
+}  // extern "C"

@@ -1,0 +1,76 @@
+// gla_internal.h - interfaces between the C ABI layer (api.cu) and the kernel
+// launchers.  Not installed; not part of the ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace gla {
+
+// Everything a decode launch needs besides pointers checked by the caller.
+struct DecodeRequest {
+  int dtype;                   // GLA_DTYPE_F32 / GLA_DTYPE_F16
+  const float* q;
+  const void* k;
+  const void* v;
+  const void* const* k_ptrs;
+  const void* const* v_ptrs;
+  int64_t kv_stride;
+  const int32_t* n_pos_dev;
+  int32_t n_pos;               // scalar rows (n_pos_dev == nullptr)
+  int32_t n_pos_add;
+  int32_t n_pos_cap;
+  int32_t max_n_pos;           // host bound used to choose the tile
+  int32_t batch;
+  int32_t n_heads;
+  int32_t n_kv;
+  int32_t head_dim;
+  float scale;
+  float* out;
+  int32_t record_mode;
+};
+
+// Launch geometry chosen for a request.
+struct DecodePlan {
+  int32_t tile;
+  int32_t stages;
+  int32_t grid;
+  int32_t threads;
+  size_t smem;
+  size_t part_floats;          // workspace floats for piece slots
+  size_t counters;             // workspace counters
+};
+
+// Device properties a plan depends on.
+struct DeviceInfo {
+  int sms;
+  int smem_optin;              // max dynamic shared memory per block
+};
+
+// Fills `plan` for `req`; returns GLA_OK or an error code with *err set.
+int plan_decode(const DecodeRequest& req, const DeviceInfo& dev, DecodePlan* plan,
+                std::string* err);
+
+// Launches the decode kernel with a plan from plan_decode.
+int launch_decode(const DecodeRequest& req, const DecodePlan& plan, float* ws_part,
+                  int32_t* ws_counter, int32_t* status, cudaStream_t stream, std::string* err);
+
+// Log-sum-exp merge of records [n_parts][n_heads][head_dim+2] into xb.
+int launch_lse_combine(const float* parts, int32_t n_parts, int32_t n_heads, int32_t head_dim,
+                       float* xb, cudaStream_t stream, std::string* err);
+
+// RoPE rotation of q/k at *position_holder followed by the KV append.
+int launch_rope_append_f32(float* q, float* k, const float* v, float* key_cache,
+                           float* value_cache, int32_t n_heads, int32_t n_kv_heads,
+                           int32_t head_dim, const int32_t* position_holder, float theta,
+                           int32_t rope_style, cudaStream_t stream, std::string* err);
+
+// Causal prefill (tcgen05).
+int launch_prefill_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v, float* out,
+                       int32_t L, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                       float scale, int32_t* status, const DeviceInfo& dev, cudaStream_t stream,
+                       std::string* err);
+
+}  // namespace gla

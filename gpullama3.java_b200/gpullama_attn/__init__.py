@@ -1,0 +1,288 @@
+"""ctypes binding of libgpullama_attn (the C ABI in include/gpullama_attn.h).
+
+This is the Python counterpart of the Java 21 FFM binding a GPULlama3.java
+maintainer adds: every call goes through the exported C symbols with raw
+device pointers.  Tensors may be passed as torch CUDA tensors (their
+``data_ptr()`` is used) or as integer device addresses.
+
+There is no fallback: importing this module fails loudly when the shared
+library has not been built (``python gpullama3.java_b200/build_lib.py``).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+
+__all__ = ["GlaError", "Context", "lib", "LIB_PATH", "DTYPE_F32", "DTYPE_F16",
+           "ROPE_INTERLEAVED", "ROPE_NEOX", "EXPORTED_SYMBOLS", "debug_partition"]
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libgpullama_attn.so")
+
+GLA_OK = 0
+DTYPE_F32 = 0
+DTYPE_F16 = 1
+ROPE_INTERLEAVED = 0
+ROPE_NEOX = 1
+
+STATUS_NAMES = {
+    0: "GLA_OK", -1: "GLA_ERR_INVALID_ARG", -2: "GLA_ERR_CUDA", -3: "GLA_ERR_NOT_SUPPORTED",
+    -4: "GLA_ERR_ALIGNMENT", -5: "GLA_ERR_TIMEOUT", -6: "GLA_ERR_COMM", -7: "GLA_ERR_NO_DEVICE",
+    -8: "GLA_ERR_OUT_OF_MEMORY",
+}
+
+_P = ctypes.c_void_p
+_I32 = ctypes.c_int32
+_I64 = ctypes.c_int64
+_F = ctypes.c_float
+
+# name -> (restype, argtypes); the list mirrors include/gpullama_attn.h
+_SIGS = {
+    "gla_version": (_I32, []),
+    "gla_status_string": (ctypes.c_char_p, [_I32]),
+    "gla_create": (_I32, [_I32, _P, ctypes.POINTER(_P)]),
+    "gla_destroy": (_I32, [_P]),
+    "gla_set_stream": (_I32, [_P, _P]),
+    "gla_last_error": (ctypes.c_char_p, [_P]),
+    "gla_device_status": (_I32, [_P, ctypes.POINTER(_I32)]),
+    "gla_reserve": (_I32, [_P, _I32, _I32, _I32, _I32]),
+    "gla_num_sms": (_I32, [_P]),
+    "gla_kv_cache_alloc": (_I32, [_P, _I32, _I32, _I32, _I32, ctypes.POINTER(_P),
+                                  ctypes.POINTER(_P)]),
+    "gla_kv_cache_free": (_I32, [_P, _P, _P]),
+    "gla_process_heads_flash_attention": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _P,
+                                                 _I32, _I32]),
+    "gla_process_heads_flash_attention_f16kv": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I32,
+                                                       _P, _I32, _I32]),
+    "gla_decode_f32kv": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F]),
+    "gla_decode_f16kv": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F]),
+    "gla_decode_batched_f32kv": (_I32, [_P, _P, _P, _P, _P, _I32, _P, _I32, _I32, _I32, _I32,
+                                        _I64, _F]),
+    "gla_decode_batched_f16kv": (_I32, [_P, _P, _P, _P, _P, _I32, _P, _I32, _I32, _I32, _I32,
+                                        _I64, _F]),
+    "gla_decode_partial_f32kv": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F]),
+    "gla_decode_partial_f16kv": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F]),
+    "gla_lse_combine": (_I32, [_P, _P, _I32, _I32, _I32, _P]),
+    "gla_comm_unique_id_size": (_I32, []),
+    "gla_comm_get_unique_id": (_I32, [_P]),
+    "gla_comm_init": (_I32, [_P, _I32, _I32, _P]),
+    "gla_decode_sharded_f16kv": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F]),
+    "gla_decode_sharded_f32kv": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F]),
+    "gla_prefill_causal_f16": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _F]),
+    "gla_rope_append_f32": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P, _F, _I32]),
+    "gla_debug_partition": (_I64, [_P, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _I64]),
+}
+
+EXPORTED_SYMBOLS = tuple(_SIGS)
+
+_lib = None
+
+
+def lib():
+    """Loads the shared library (raises ImportError when it is missing)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with python gpullama3.java_b200/build_lib.py")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+class GlaError(RuntimeError):
+    """A libgpullama_attn call returned a negative status."""
+
+    def __init__(self, status: int, message: str):
+        self.status = status
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+
+
+def _ptr(x) -> int | None:
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    dp = getattr(x, "data_ptr", None)
+    if dp is not None:
+        return int(dp())
+    raise TypeError(f"expected a device tensor or an address, got {type(x)!r}")
+
+
+def debug_partition(n_pos, n_kv_heads, tile, n_ctas):
+    """Host run of the decode work partition (no GPU). Returns a dict of lists."""
+    import numpy as np
+
+    n_pos = np.ascontiguousarray(n_pos, dtype=np.int32)
+    total = int(sum((max(int(x), 0) + tile - 1) // tile for x in n_pos)) * n_kv_heads
+    cap = max(total, 1)
+    arrs = [np.zeros(cap, dtype=np.int32) for _ in range(5)]
+    rc = lib().gla_debug_partition(n_pos.ctypes.data, len(n_pos), n_kv_heads, tile, n_ctas,
+                                   *[a.ctypes.data for a in arrs], cap)
+    if rc < 0:
+        raise GlaError(int(rc), "gla_debug_partition")
+    names = ("cta", "seq", "kv_head", "row0", "slot")
+    return {k: a[:rc] for k, a in zip(names, arrs)}
+
+
+class Context:
+    """Owns one gla_ctx (device, stream, workspace)."""
+
+    def __init__(self, device: int = 0, stream=None):
+        self._L = lib()
+        self._h = _P()
+        if stream is None:
+            try:
+                import torch
+
+                stream = torch.cuda.current_stream(device).cuda_stream
+            except Exception:  # pragma: no cover - torch without CUDA
+                stream = 0
+        rc = self._L.gla_create(device, _P(int(stream) if stream else None), ctypes.byref(self._h))
+        if rc != GLA_OK:
+            raise GlaError(rc, "gla_create failed")
+        self.device = device
+
+    # -- plumbing ---------------------------------------------------------
+    def _check(self, rc: int, what: str):
+        if rc != GLA_OK:
+            msg = self._L.gla_last_error(self._h)
+            raise GlaError(rc, f"{what}: {msg.decode() if msg else ''}")
+
+    def close(self):
+        if self._h:
+            self._L.gla_destroy(self._h)
+            self._h = _P()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    def set_stream(self, stream):
+        self._check(self._L.gla_set_stream(self._h, _P(int(stream) if stream else None)),
+                    "gla_set_stream")
+
+    def num_sms(self) -> int:
+        return int(self._L.gla_num_sms(self._h))
+
+    def device_status(self) -> int:
+        st = _I32(0)
+        self._check(self._L.gla_device_status(self._h, ctypes.byref(st)), "gla_device_status")
+        return int(st.value)
+
+    def reserve(self, max_batch, max_kv_heads, max_heads, max_head_dim):
+        self._check(self._L.gla_reserve(self._h, max_batch, max_kv_heads, max_heads, max_head_dim),
+                    "gla_reserve")
+
+    # -- KV cache ---------------------------------------------------------
+    def kv_cache_alloc(self, n_layers, context_length, kv_dim, dtype=DTYPE_F32):
+        k, v = _P(), _P()
+        self._check(self._L.gla_kv_cache_alloc(self._h, n_layers, context_length, kv_dim, dtype,
+                                               ctypes.byref(k), ctypes.byref(v)),
+                    "gla_kv_cache_alloc")
+        return k.value, v.value
+
+    def kv_cache_free(self, k, v):
+        self._check(self._L.gla_kv_cache_free(self._h, _P(k), _P(v)), "gla_kv_cache_free")
+
+    # -- the reference task -------------------------------------------------
+    def process_heads_flash_attention(self, q, key_cache, value_cache, xb, n_heads, head_size,
+                                      kv_dim, kv_mul, position_holder, layer, context_length,
+                                      f16_cache=False):
+        fn = (self._L.gla_process_heads_flash_attention_f16kv if f16_cache
+              else self._L.gla_process_heads_flash_attention)
+        self._check(fn(self._h, _ptr(q), _ptr(key_cache), _ptr(value_cache), _ptr(xb), n_heads,
+                       head_size, kv_dim, kv_mul, _ptr(position_holder), layer, context_length),
+                    "gla_process_heads_flash_attention")
+
+    # -- decode -------------------------------------------------------------
+    def decode(self, q, k, v, xb, n_heads, n_kv_heads, head_dim, n_pos, scale=None,
+               kv_stride=None, f16_cache=False):
+        if scale is None:
+            scale = 1.0 / math.sqrt(head_dim)
+        if kv_stride is None:
+            kv_stride = n_kv_heads * head_dim
+        fn = self._L.gla_decode_f16kv if f16_cache else self._L.gla_decode_f32kv
+        self._check(fn(self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(xb), n_heads, n_kv_heads,
+                       head_dim, kv_stride, n_pos, scale), "gla_decode")
+
+    def decode_partial(self, q, k, v, part, n_heads, n_kv_heads, head_dim, n_pos, scale=None,
+                       kv_stride=None, f16_cache=False):
+        if scale is None:
+            scale = 1.0 / math.sqrt(head_dim)
+        if kv_stride is None:
+            kv_stride = n_kv_heads * head_dim
+        fn = self._L.gla_decode_partial_f16kv if f16_cache else self._L.gla_decode_partial_f32kv
+        self._check(fn(self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(part), n_heads, n_kv_heads,
+                       head_dim, kv_stride, n_pos, scale), "gla_decode_partial")
+
+    def decode_batched(self, q, k_ptrs, v_ptrs, n_pos, max_n_pos, xb, batch, n_heads,
+                       n_kv_heads, head_dim, scale=None, kv_stride=None, f16_cache=False):
+        if scale is None:
+            scale = 1.0 / math.sqrt(head_dim)
+        if kv_stride is None:
+            kv_stride = n_kv_heads * head_dim
+        fn = self._L.gla_decode_batched_f16kv if f16_cache else self._L.gla_decode_batched_f32kv
+        self._check(fn(self._h, _ptr(q), _ptr(k_ptrs), _ptr(v_ptrs), _ptr(n_pos), max_n_pos,
+                       _ptr(xb), batch, n_heads, n_kv_heads, head_dim, kv_stride, scale),
+                    "gla_decode_batched")
+
+    def lse_combine(self, parts, n_parts, n_heads, head_dim, xb):
+        self._check(self._L.gla_lse_combine(self._h, _ptr(parts), n_parts, n_heads, head_dim,
+                                            _ptr(xb)), "gla_lse_combine")
+
+    # -- multi-GPU ----------------------------------------------------------
+    @staticmethod
+    def comm_unique_id() -> bytes:
+        L = lib()
+        n = L.gla_comm_unique_id_size()
+        buf = ctypes.create_string_buffer(n)
+        rc = L.gla_comm_get_unique_id(buf)
+        if rc != GLA_OK:
+            raise GlaError(rc, "gla_comm_get_unique_id")
+        return buf.raw
+
+    def comm_init(self, nranks: int, rank: int, unique_id: bytes):
+        buf = ctypes.create_string_buffer(unique_id, len(unique_id))
+        self._check(self._L.gla_comm_init(self._h, nranks, rank, buf), "gla_comm_init")
+
+    def decode_sharded(self, q, k, v, xb, n_heads, n_kv_heads, head_dim, n_pos_local,
+                       scale=None, kv_stride=None, f16_cache=True):
+        if scale is None:
+            scale = 1.0 / math.sqrt(head_dim)
+        if kv_stride is None:
+            kv_stride = n_kv_heads * head_dim
+        fn = self._L.gla_decode_sharded_f16kv if f16_cache else self._L.gla_decode_sharded_f32kv
+        self._check(fn(self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(xb), n_heads, n_kv_heads,
+                       head_dim, kv_stride, n_pos_local, scale), "gla_decode_sharded")
+
+    # -- prefill / producers --------------------------------------------------
+    def prefill_causal(self, q, k, v, out, L, n_heads, n_kv_heads, head_dim, scale=None):
+        if scale is None:
+            scale = 1.0 / math.sqrt(head_dim)
+        self._check(self._L.gla_prefill_causal_f16(self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(out),
+                                                   L, n_heads, n_kv_heads, head_dim, scale),
+                    "gla_prefill_causal_f16")
+
+    def rope_append(self, q, k, v, key_cache, value_cache, n_heads, n_kv_heads, head_dim,
+                    position_holder, theta, style=ROPE_INTERLEAVED):
+        self._check(self._L.gla_rope_append_f32(self._h, _ptr(q), _ptr(k), _ptr(v),
+                                                _ptr(key_cache), _ptr(value_cache), n_heads,
+                                                n_kv_heads, head_dim, _ptr(position_holder),
+                                                theta, style), "gla_rope_append_f32")

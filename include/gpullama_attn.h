@@ -1,0 +1,280 @@
+/*
+ * gpullama_attn.h - C ABI of libgpullama_attn, a B200 (sm_100a) attention
+ * library that replaces the per-layer attention task of GPULlama3.java.
+ *
+ * Conventions (all entry points):
+ *  - Every tensor pointer is a caller-owned DEVICE pointer on the context's
+ *    device (Java passes MemorySegment.address() of a device segment).
+ *  - Calls are asynchronous and ordered on the context's CUDA stream.
+ *  - Return value: GLA_OK (0) or a negative GLA_ERR_* code.  Nothing aborts and
+ *    no C++ exception crosses the ABI.  gla_last_error() describes the last
+ *    failure of a context.  Errors found by a kernel while it runs (a bounded
+ *    wait that gave up) are latched in a device status word that
+ *    gla_device_status() reads back.
+ *  - A context is not thread-safe: use one per (device, host thread).
+ *  - All element offsets are 64-bit.
+ *  - Layouts follow the reference:
+ *      q   [n_heads][head_dim]              FP32 (one token)
+ *      K/V [position][kv_stride] per layer  (kv_stride = n_kv_heads*head_dim
+ *                                            for the reference layout)
+ *      xb  [n_heads][head_dim]              FP32
+ *    q head h reads kv head h / (n_heads / n_kv_heads)  (GQA, kvMul).
+ *  - FP16 tensors are IEEE binary16 passed as uint16_t.
+ */
+#ifndef GPULLAMA_ATTN_H
+#define GPULLAMA_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GLA_VERSION 100 /* 1.0.0 */
+
+/* status codes */
+#define GLA_OK 0
+#define GLA_ERR_INVALID_ARG (-1)   /* null pointer, bad size, bad shape        */
+#define GLA_ERR_CUDA (-2)          /* a CUDA runtime call failed              */
+#define GLA_ERR_NOT_SUPPORTED (-3) /* shape outside the compiled variants      */
+#define GLA_ERR_ALIGNMENT (-4)     /* pointer/stride not 16-byte aligned       */
+#define GLA_ERR_TIMEOUT (-5)       /* a bounded device or host wait gave up    */
+#define GLA_ERR_COMM (-6)          /* NCCL failure or communicator missing     */
+#define GLA_ERR_NO_DEVICE (-7)     /* no CUDA device / wrong device id         */
+#define GLA_ERR_OUT_OF_MEMORY (-8) /* device allocation failed                 */
+
+/* element types */
+#define GLA_DTYPE_F32 0
+#define GLA_DTYPE_F16 1
+
+typedef struct gla_ctx gla_ctx;
+
+/* ------------------------------------------------------------------------ */
+/* Library / context                                                         */
+/* ------------------------------------------------------------------------ */
+
+/* Library version (GLA_VERSION of the build). */
+int32_t gla_version(void);
+
+/* Human-readable name of a status code (static string). */
+const char* gla_status_string(int32_t status);
+
+/* Creates a context on `device` that launches on `cuda_stream` (a cudaStream_t;
+ * NULL = the legacy default stream).  Allocates the context's device
+ * workspace.  Replaces the per-plan device set-up of
+ * tornadovm/TornadoVMMasterPlan.java:37-79 (initializeTornadoVMPlan) for the
+ * attention task. */
+int32_t gla_create(int32_t device, void* cuda_stream, gla_ctx** out);
+
+/* Frees the context, its workspace and its communicator (if any). */
+int32_t gla_destroy(gla_ctx* ctx);
+
+/* Re-targets the context to another stream of the same device. */
+int32_t gla_set_stream(gla_ctx* ctx, void* cuda_stream);
+
+/* Message of the context's last failure ("" if none).  Valid until the next
+ * call on the context. */
+const char* gla_last_error(const gla_ctx* ctx);
+
+/* Synchronises the context's stream, then returns (and clears) the device
+ * status word that kernels set when a bounded wait gives up
+ * (GLA_OK or GLA_ERR_TIMEOUT), or GLA_ERR_CUDA if the stream itself failed. */
+int32_t gla_device_status(gla_ctx* ctx, int32_t* device_status);
+
+/* Grows the context workspace so that later decode calls of up to
+ * `max_batch` sequences x `max_kv_heads` KV heads x `max_heads` q heads of
+ * `max_head_dim` never allocate (call before CUDA-graph capture). */
+int32_t gla_reserve(gla_ctx* ctx, int32_t max_batch, int32_t max_kv_heads, int32_t max_heads,
+                    int32_t max_head_dim);
+
+/* Number of streaming multiprocessors of the context's device. */
+int32_t gla_num_sms(const gla_ctx* ctx);
+
+/* ------------------------------------------------------------------------ */
+/* KV cache allocation (device MemorySegments of State)                      */
+/* ------------------------------------------------------------------------ */
+
+/* Allocates zero-initialised key and value caches of
+ * n_layers * context_length * kv_dim elements of `dtype` each, laid out
+ * [layer][position][kv_dim] like the flat wrapKeyCache/wrapValueCache of the
+ * reference (inference/state/LlamaState.java:61-64, State.java:56-57), with
+ * the per-layer CPU layout [position][kv_dim] (State.java:41-42) as each
+ * layer's slice.  Replaces the zero-initialised host arrays that TornadoVM
+ * copies to the device once (layers/type/fp16/LlamaFP16FFNLayers.java:145-165). */
+int32_t gla_kv_cache_alloc(gla_ctx* ctx, int32_t n_layers, int32_t context_length, int32_t kv_dim,
+                           int32_t dtype, void** key_cache, void** value_cache);
+
+/* Frees caches from gla_kv_cache_alloc. */
+int32_t gla_kv_cache_free(gla_ctx* ctx, void* key_cache, void* value_cache);
+
+/* ------------------------------------------------------------------------ */
+/* The reference task, argument for argument                                 */
+/* ------------------------------------------------------------------------ */
+
+/* Drop-in for the TornadoVM task "parallel-attention"
+ *   TransformerComputeKernelsLayered.processHeadsFlashAttention(
+ *       context, q, key_cache, value_cache, xb, nHeads, headSize, kvDim, kvMul,
+ *       positionHolder, layer, contextLength)
+ * (tornadovm/kernels/TransformerComputeKernelsLayered.java:336-458, wired at
+ * tornadovm/layers/type/fp16/LlamaFP16FFNLayers.java:167-177).
+ *  key_cache/value_cache: flat FP32 [layer][contextLength][kvDim] caches.
+ *  position_holder: DEVICE int32 whose element 0 is the current position
+ *  (IntArray positionHolder, State.java:58); attention covers positions
+ *  0..position inclusive.  Scale is 1/sqrt(headSize) (InferenceCore.java:65,121).
+ *  Because the position is read on the device, the call can be captured in a
+ *  CUDA graph and replayed for every token. */
+int32_t gla_process_heads_flash_attention(gla_ctx* ctx, const float* q, const float* key_cache,
+                                          const float* value_cache, float* xb, int32_t n_heads,
+                                          int32_t head_size, int32_t kv_dim, int32_t kv_mul,
+                                          const int32_t* position_holder, int32_t layer,
+                                          int32_t context_length);
+
+/* Same task over an FP16 cache (new capability; the reference KV is FP32). */
+int32_t gla_process_heads_flash_attention_f16kv(gla_ctx* ctx, const float* q,
+                                                const uint16_t* key_cache,
+                                                const uint16_t* value_cache, float* xb,
+                                                int32_t n_heads, int32_t head_size, int32_t kv_dim,
+                                                int32_t kv_mul, const int32_t* position_holder,
+                                                int32_t layer, int32_t context_length);
+
+/* ------------------------------------------------------------------------ */
+/* Decode attention (one new token per sequence), explicit pointers          */
+/* ------------------------------------------------------------------------ */
+
+/* Single-sequence decode over an FP32 cache.  k/v point at the LAYER base
+ * (row 0); row t of kv head g starts at k + t*kv_stride + g*head_dim.
+ * n_pos = position + 1 rows are attended.  scale multiplies q.k (the
+ * reference divides by sqrt(head_dim): InferenceCore.java:121).
+ * Replaces the CPU block InferenceCore.java:105-144 (forwardJava; also
+ * forwardJavaQwen2 :233-272, forwardJavaQwen3 :375-407, forwardJavaPhi3
+ * :495-517) and the GPU kernels TransformerComputeKernelsLayered.java:336-458,
+ * :463-628, :278-334/:1091-1103, Qwen2Kernels.java:10-130,
+ * Qwen3Kernels.java:193-293. */
+int32_t gla_decode_f32kv(gla_ctx* ctx, const float* q, const float* k, const float* v, float* xb,
+                         int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int64_t kv_stride,
+                         int32_t n_pos, float scale);
+
+/* Same over an FP16 cache; FP32 softmax and accumulation. */
+int32_t gla_decode_f16kv(gla_ctx* ctx, const float* q, const uint16_t* k, const uint16_t* v,
+                         float* xb, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                         int64_t kv_stride, int32_t n_pos, float scale);
+
+/* Batched decode: `batch` independent sequences, one new token each.
+ *  q  [batch][n_heads][head_dim], xb [batch][n_heads][head_dim]
+ *  k_ptrs/v_ptrs: DEVICE arrays of `batch` layer-base pointers
+ *  n_pos: DEVICE int32 array [batch] (rows attended per sequence, >= 1)
+ *  max_n_pos: host upper bound of n_pos[] (used only to pick the tile size).
+ * No reference counterpart for batch > 1 (the reference decodes one
+ * sequence: inference/InferenceEngine.java:67-141); each sequence computes
+ * exactly what gla_decode_*kv computes for it. */
+int32_t gla_decode_batched_f32kv(gla_ctx* ctx, const float* q, const float* const* k_ptrs,
+                                 const float* const* v_ptrs, const int32_t* n_pos,
+                                 int32_t max_n_pos, float* xb, int32_t batch, int32_t n_heads,
+                                 int32_t n_kv_heads, int32_t head_dim, int64_t kv_stride,
+                                 float scale);
+int32_t gla_decode_batched_f16kv(gla_ctx* ctx, const float* q, const uint16_t* const* k_ptrs,
+                                 const uint16_t* const* v_ptrs, const int32_t* n_pos,
+                                 int32_t max_n_pos, float* xb, int32_t batch, int32_t n_heads,
+                                 int32_t n_kv_heads, int32_t head_dim, int64_t kv_stride,
+                                 float scale);
+
+/* Partial decode over one contiguous KV shard (rows [0, n_pos) of k/v, which
+ * hold some range of the global sequence).  Instead of xb it writes, per q
+ * head h, the record part[h][0..head_dim+2):
+ *     part[h][0..head_dim)  = sum_t exp(s_t - m) v_t / l   (normalised o)
+ *     part[h][head_dim]     = m = max_t s_t                (natural log units)
+ *     part[h][head_dim + 1] = l = sum_t exp(s_t - m)
+ * where s_t = scale * q_h . k_t.  Records of disjoint shards merge exactly
+ * with gla_lse_combine.  No reference counterpart (the reference is single
+ * device, SchedulerDetectionService.java:13-26). */
+int32_t gla_decode_partial_f32kv(gla_ctx* ctx, const float* q, const float* k, const float* v,
+                                 float* part, int32_t n_heads, int32_t n_kv_heads,
+                                 int32_t head_dim, int64_t kv_stride, int32_t n_pos, float scale);
+int32_t gla_decode_partial_f16kv(gla_ctx* ctx, const float* q, const uint16_t* k,
+                                 const uint16_t* v, float* part, int32_t n_heads,
+                                 int32_t n_kv_heads, int32_t head_dim, int64_t kv_stride,
+                                 int32_t n_pos, float scale);
+
+/* Log-sum-exp merge of `n_parts` record sets parts[n_parts][n_heads][head_dim+2]
+ * (layout above) into xb[n_heads][head_dim]:
+ *     M = max_i m_i,  w_i = l_i exp(m_i - M),  xb = sum_i w_i o_i / sum_i w_i.
+ * Records with l = 0 (empty shards) are ignored. */
+int32_t gla_lse_combine(gla_ctx* ctx, const float* parts, int32_t n_parts, int32_t n_heads,
+                        int32_t head_dim, float* xb);
+
+/* ------------------------------------------------------------------------ */
+/* Multi-GPU: KV-sequence sharded decode over NCCL                           */
+/* ------------------------------------------------------------------------ */
+
+/* Size in bytes of the opaque unique id used by gla_comm_init (ncclUniqueId). */
+int32_t gla_comm_unique_id_size(void);
+
+/* Writes a fresh unique id (rank 0 creates it and shares it out of band). */
+int32_t gla_comm_get_unique_id(void* unique_id);
+
+/* Joins an NCCL communicator of `nranks` ranks, one per GPU. */
+int32_t gla_comm_init(gla_ctx* ctx, int32_t nranks, int32_t rank, const void* unique_id);
+
+/* Decode of one sequence whose KV rows are sharded across the communicator's
+ * ranks (this rank holds n_pos_local rows).  Every rank computes its partial
+ * record set, all-gathers the sets over NCCL and merges them: every rank ends
+ * with the full xb.  Needs gla_comm_init first. */
+int32_t gla_decode_sharded_f16kv(gla_ctx* ctx, const float* q, const uint16_t* k,
+                                 const uint16_t* v, float* xb, int32_t n_heads,
+                                 int32_t n_kv_heads, int32_t head_dim, int64_t kv_stride,
+                                 int32_t n_pos_local, float scale);
+int32_t gla_decode_sharded_f32kv(gla_ctx* ctx, const float* q, const float* k, const float* v,
+                                 float* xb, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                 int64_t kv_stride, int32_t n_pos_local, float scale);
+
+/* ------------------------------------------------------------------------ */
+/* Causal prefill (tcgen05 / TMEM)                                           */
+/* ------------------------------------------------------------------------ */
+
+/* Causal attention of a whole prompt: for every row p in [0, L) and head h,
+ *   out[p][h] = softmax_t<=p(scale * q[p][h] . k[t][h/kvMul]) . v[t][h/kvMul]
+ * q [L][n_heads*head_dim], k/v [L][n_kv_heads*head_dim] FP16 (row strides are
+ * the packed widths), out [L][n_heads*head_dim] FP32.  Mathematically the
+ * reference's prompt ingestion, which runs decode attention at positions
+ * 0..L-1 one token at a time (inference/InferenceEngine.java:88-99, :309-327). */
+int32_t gla_prefill_causal_f16(gla_ctx* ctx, const uint16_t* q, const uint16_t* k,
+                               const uint16_t* v, float* out, int32_t L, int32_t n_heads,
+                               int32_t n_kv_heads, int32_t head_dim, float scale);
+
+/* ------------------------------------------------------------------------ */
+/* Input producers: RoPE + KV append (the step before attention)             */
+/* ------------------------------------------------------------------------ */
+
+#define GLA_ROPE_INTERLEAVED 0 /* Llama/Mistral: pairs (2i, 2i+1), InferenceCore.java:82-94   */
+#define GLA_ROPE_NEOX 1        /* Qwen2/Qwen3/Phi3: pairs (i, i+hd/2), InferenceCore.java:210-225 */
+
+/* Rotates q (n_heads heads) and k (n_kv_heads heads) in place for `position`
+ * with frequencies 1/theta^(2i/head_dim) (RoPE.java:6-37 without Llama-3.1
+ * scaling), then appends k and v as row `position` of the FP32 layer caches
+ * key_cache/value_cache ([position][kv_dim], InferenceCore.java:99-100;
+ * copyToCache TransformerComputeKernelsLayered.java:129-139).  position is
+ * read from the DEVICE int32 position_holder[0]. */
+int32_t gla_rope_append_f32(gla_ctx* ctx, float* q, float* k, const float* v, float* key_cache,
+                            float* value_cache, int32_t n_heads, int32_t n_kv_heads,
+                            int32_t head_dim, const int32_t* position_holder, float theta,
+                            int32_t rope_style);
+
+/* ------------------------------------------------------------------------ */
+/* Introspection used by the host tests (no device work)                     */
+/* ------------------------------------------------------------------------ */
+
+/* Runs the decode kernels' work partition on the host: `n_seq` sequences with
+ * n_pos[] rows, n_kv_heads segments each, tiles of `tile` rows over `n_ctas`
+ * CTAs.  Writes for every tile (in work order) its CTA, sequence, kv head,
+ * first row and partial-slot index into the five arrays (each of length
+ * `capacity`); returns the tile count or a negative status. */
+int64_t gla_debug_partition(const int32_t* n_pos, int32_t n_seq, int32_t n_kv_heads, int32_t tile,
+                            int32_t n_ctas, int32_t* cta, int32_t* seq, int32_t* kv_head,
+                            int32_t* row0, int32_t* slot, int64_t capacity);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GPULLAMA_ATTN_H */

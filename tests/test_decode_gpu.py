@@ -1,0 +1,291 @@
+"""Decode attention on the GPU (through the C ABI) against the CPU oracle.
+
+Tolerances: max |err| <= 1e-3 and max |err| / max |ref|
+<= 1e-3 with an FP32 cache; 5e-3 for both with an FP16 cache.
+"""
+import math
+
+import numpy as np
+import pytest
+
+import inputs
+import reference64
+
+pytestmark = pytest.mark.gpu
+
+TOL_F32 = 1e-3
+TOL_F16 = 5e-3
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def dev(x):
+    torch = _torch()
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def assert_close(got, ref, tol, what=""):
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    err = np.abs(got - ref).max()
+    scale = max(np.abs(ref).max(), 1e-30)
+    assert err <= tol and err / scale <= tol, f"{what}: max abs err {err:.3e}, rel {err / scale:.3e}"
+
+
+def gpu_decode(ctx, q, k, v, nh, nkv, hd, n_pos, f16=False, kv_stride=None):
+    torch = _torch()
+    if f16:
+        k, v = inputs.to_f16_bits(k), inputs.to_f16_bits(v)
+    qd, kd, vd = dev(q), dev(k.view(np.int16) if f16 else k), dev(v.view(np.int16) if f16 else v)
+    xb = torch.empty(nh * hd, dtype=torch.float32, device="cuda")
+    ctx.decode(qd, kd, vd, xb, nh, nkv, hd, n_pos, kv_stride=kv_stride, f16_cache=f16)
+    assert ctx.device_status() == 0
+    return xb.cpu().numpy(), k, v
+
+
+SWEEP_POS = [0, 1, 7, 8, 31, 32, 33, 511, 4095]
+
+
+@pytest.mark.parametrize("f16", [False, True], ids=["f32kv", "f16kv"])
+@pytest.mark.parametrize("hd", [64, 96, 128])
+@pytest.mark.parametrize("kv_mul", [1, 3, 4, 7, 8])
+def test_decode_sweep(gla_ctx, oracle, f16, hd, kv_mul):
+    nkv = 2
+    nh = nkv * kv_mul
+    n_rows = max(SWEEP_POS) + 1
+    q, k, v = inputs.decode_case(1000 + hd + kv_mul, nh, nkv, hd, n_rows)
+    for pos in SWEEP_POS:
+        xb, kk, vv = gpu_decode(gla_ctx, q, k, v, nh, nkv, hd, pos + 1, f16=f16)
+        if f16:
+            ref = oracle.decode_f16(q, kk, vv, nh, nkv, hd, pos + 1)
+        else:
+            ref = oracle.decode_f32(q, k, v, nh, nkv, hd, pos + 1)
+        assert_close(xb, ref, TOL_F16 if f16 else TOL_F32, f"pos={pos}")
+
+
+def test_golden_fixtures_on_gpu(gla_ctx):
+    import os
+
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "attention_golden.npz"))
+    names = sorted({k.split("/")[0] for k in g.files if k.endswith("/xb")})
+    for name in names:
+        seed, nh, nkv, hd, npos, f16 = (int(x) for x in g[f"{name}/meta"])
+        if f"{name}/q" in g.files:
+            q, k, v = g[f"{name}/q"], g[f"{name}/k"], g[f"{name}/v"]
+            if f16:
+                k = k.view(np.float16).astype(np.float32)
+                v = v.view(np.float16).astype(np.float32)
+        else:
+            q, k, v = inputs.decode_case(seed, nh, nkv, hd, npos)
+        xb, _, _ = gpu_decode(gla_ctx, q, k, v, nh, nkv, hd, npos, f16=bool(f16))
+        assert_close(xb, g[f"{name}/xb"], TOL_F16 if f16 else TOL_F32, name)
+
+
+def test_c1_llama32_1b_exact_config(gla_ctx, oracle):
+    # nHeads 32, nKVHeads 8, hd 64, position 511, seed 0
+    q, k, v = inputs.decode_case(0, 32, 8, 64, 512)
+    xb, _, _ = gpu_decode(gla_ctx, q, k, v, 32, 8, 64, 512)
+    assert_close(xb, oracle.decode_f32(q, k, v, 32, 8, 64, 512), TOL_F32, "C1")
+
+
+@pytest.mark.parametrize("f16", [False, True])
+def test_padded_kv_stride(gla_ctx, oracle, f16):
+    nh, nkv, hd, n = 8, 2, 128, 300
+    stride = nkv * hd + 64
+    q, k, v = inputs.decode_case(21, nh, nkv, hd, n, kv_stride=stride)
+    xb, kk, vv = gpu_decode(gla_ctx, q, k, v, nh, nkv, hd, n, f16=f16, kv_stride=stride)
+    if f16:
+        ref = oracle.decode_f16(q, kk, vv, nh, nkv, hd, n, kv_stride=stride)
+    else:
+        ref = oracle.decode_f32(q, k, v, nh, nkv, hd, n, kv_stride=stride)
+    assert_close(xb, ref, TOL_F16 if f16 else TOL_F32)
+
+
+def test_repeated_calls_are_identical(gla_ctx):
+    # the piece counters reset themselves: back-to-back calls agree bit for bit
+    q, k, v = inputs.decode_case(22, 24, 8, 128, 4096)
+    a, _, _ = gpu_decode(gla_ctx, q, k, v, 24, 8, 128, 4096)
+    for _ in range(3):
+        b, _, _ = gpu_decode(gla_ctx, q, k, v, 24, 8, 128, 4096)
+        np.testing.assert_array_equal(a, b)
+
+
+def test_process_heads_flash_attention_mirror(gla_ctx, oracle):
+    """The reference task signature: flat [layer][ctx][kvDim] caches, device position."""
+    torch = _torch()
+    n_layers, ctx_len, nh, nkv, hd = 3, 256, 16, 4, 64
+    kv_dim = nkv * hd
+    rng = np.random.Generator(np.random.PCG64(23))
+    kc = rng.standard_normal((n_layers, ctx_len, kv_dim), dtype=np.float32)
+    vc = rng.standard_normal((n_layers, ctx_len, kv_dim), dtype=np.float32)
+    q = rng.standard_normal(nh * hd, dtype=np.float32)
+    kd, vd, qd = dev(kc), dev(vc), dev(q)
+    xb = torch.empty(nh * hd, device="cuda")
+    for layer in range(n_layers):
+        for pos in (0, 100, ctx_len - 1):
+            ph = torch.tensor([pos], dtype=torch.int32, device="cuda")
+            gla_ctx.process_heads_flash_attention(qd, kd, vd, xb, nh, hd, kv_dim, nh // nkv, ph,
+                                                  layer, ctx_len)
+            assert gla_ctx.device_status() == 0
+            ref = oracle.decode_f32(q, kc[layer], vc[layer], nh, nkv, hd, pos + 1)
+            assert_close(xb.cpu().numpy(), ref, TOL_F32, f"layer {layer} pos {pos}")
+
+
+def test_process_heads_position_beyond_context_is_latched(gla_ctx):
+    torch = _torch()
+    nh, nkv, hd, ctx_len = 8, 2, 64, 64
+    kd = torch.zeros(ctx_len, nkv * hd, device="cuda")
+    vd = torch.zeros_like(kd)
+    qd = torch.zeros(nh * hd, device="cuda")
+    xb = torch.empty_like(qd)
+    ph = torch.tensor([ctx_len + 5], dtype=torch.int32, device="cuda")
+    gla_ctx.process_heads_flash_attention(qd, kd, vd, xb, nh, hd, nkv * hd, nh // nkv, ph, 0,
+                                          ctx_len)
+    assert gla_ctx.device_status() == -1  # GLA_ERR_INVALID_ARG, rows clamped to the cache
+    assert gla_ctx.device_status() == 0   # cleared by the read
+
+
+@pytest.mark.parametrize("f16", [False, True])
+def test_batched_ragged(gla_ctx, oracle, f16):
+    torch = _torch()
+    nh, nkv, hd = 32, 8, 128
+    lengths = [1, 17, 64, 65, 1000, 3333, 128]
+    B = len(lengths)
+    qs, ks, vs, refs = [], [], [], []
+    for b, n in enumerate(lengths):
+        q, k, v = inputs.decode_case(300 + b, nh, nkv, hd, n)
+        if f16:
+            k16, v16 = inputs.to_f16_bits(k), inputs.to_f16_bits(v)
+            refs.append(oracle.decode_f16(q, k16, v16, nh, nkv, hd, n))
+            ks.append(dev(k16.view(np.int16)))
+            vs.append(dev(v16.view(np.int16)))
+        else:
+            refs.append(oracle.decode_f32(q, k, v, nh, nkv, hd, n))
+            ks.append(dev(k))
+            vs.append(dev(v))
+        qs.append(q)
+    qd = dev(np.stack(qs))
+    kp = torch.tensor([t.data_ptr() for t in ks], dtype=torch.int64, device="cuda")
+    vp = torch.tensor([t.data_ptr() for t in vs], dtype=torch.int64, device="cuda")
+    npd = torch.tensor(lengths, dtype=torch.int32, device="cuda")
+    xb = torch.empty(B, nh * hd, device="cuda")
+    gla_ctx.decode_batched(qd, kp, vp, npd, max(lengths), xb, B, nh, nkv, hd, f16_cache=f16)
+    assert gla_ctx.device_status() == 0
+    out = xb.cpu().numpy()
+    for b in range(B):
+        assert_close(out[b], refs[b], TOL_F16 if f16 else TOL_F32, f"seq {b}")
+
+
+@pytest.mark.parametrize("f16", [False, True])
+def test_partial_records_and_combine(gla_ctx, oracle, f16):
+    """KV-sequence sharding emulated on one GPU: shard records merge to the full result."""
+    torch = _torch()
+    nh, nkv, hd, n = 28, 4, 128, 5000
+    q, k, v = inputs.decode_case(31, nh, nkv, hd, n)
+    bounds = [0, 1, 1700, 3001, n]  # includes a one-row shard
+    S = len(bounds) - 1
+    parts = torch.empty(S, nh, hd + 2, device="cuda")
+    if f16:
+        k16, v16 = inputs.to_f16_bits(k), inputs.to_f16_bits(v)
+        kq = k16.view(np.float16).astype(np.float32)
+        vq = v16.view(np.float16).astype(np.float32)
+    else:
+        kq, vq = k, v
+    qd = dev(q)
+    keep = []
+    for s in range(S):
+        lo, hi = bounds[s], bounds[s + 1]
+        if f16:
+            ks = dev(k16[lo:hi].view(np.int16))
+            vs = dev(v16[lo:hi].view(np.int16))
+        else:
+            ks, vs = dev(k[lo:hi]), dev(v[lo:hi])
+        keep += [ks, vs]
+        gla_ctx.decode_partial(qd, ks, vs, parts[s], nh, nkv, hd, hi - lo, f16_cache=f16)
+        assert gla_ctx.device_status() == 0
+        rec = parts[s].cpu().numpy()
+        want = reference64.records64(q, kq, vq, nh, nkv, hd, slice(lo, hi))
+        tol = TOL_F16 if f16 else TOL_F32
+        assert_close(rec[:, :hd], want[:, :hd], tol, f"o shard {s}")
+        np.testing.assert_allclose(rec[:, hd], want[:, hd], atol=tol * 10)
+        np.testing.assert_allclose(rec[:, hd + 1], want[:, hd + 1], rtol=tol * 10)
+    xb = torch.empty(nh * hd, device="cuda")
+    gla_ctx.lse_combine(parts, S, nh, hd, xb)
+    ref = (oracle.decode_f16(q, k16, v16, nh, nkv, hd, n) if f16
+           else oracle.decode_f32(q, k, v, nh, nkv, hd, n))
+    assert_close(xb.cpu().numpy(), ref, TOL_F16 if f16 else TOL_F32, "combined")
+
+
+def test_argument_errors_with_context(gla_ctx):
+    torch = _torch()
+    import gpullama_attn as gla
+
+    q = torch.zeros(8 * 64 + 4, device="cuda")
+    k = torch.zeros(64, 128, device="cuda")
+    xb = torch.zeros(8 * 64, device="cuda")
+    with pytest.raises(gla.GlaError) as e:  # misaligned q
+        gla_ctx.decode(q.data_ptr() + 4, k, k, xb, 8, 2, 64, 10)
+    assert e.value.status == -4
+    with pytest.raises(gla.GlaError) as e:  # unsupported head_dim
+        gla_ctx.decode(q, k, k, xb, 8, 2, 80, 10, kv_stride=160)
+    assert e.value.status == -3
+    with pytest.raises(gla.GlaError) as e:  # kvMul 16 > 8
+        gla_ctx.decode(q, k, k, xb, 16, 1, 64, 10, kv_stride=128)
+    assert e.value.status == -3
+    with pytest.raises(gla.GlaError) as e:  # n_pos 0
+        gla_ctx.decode(q, k, k, xb, 8, 2, 64, 0)
+    assert e.value.status == -1
+    assert "n_pos" in str(e.value)
+    assert gla_ctx.device_status() == 0
+
+
+def test_c2_layer_full_size(gla_ctx, oracle):
+    # Llama-3.2-3B shape, context 4096, FP32 cache, RoPE'd inputs (theta 500000)
+    nh, nkv, hd, T = 24, 8, 128, 4096
+    q, k, v = inputs.decode_case(41, nh, nkv, hd, T)
+    cr, ci = oracle.rope_freqs(T, hd, 500000.0)
+    oracle.rope_interleaved(q, k[T - 1], hd, T - 1, cr, ci)  # q and the new key at pos T-1
+    scratch = np.zeros(nh * hd, np.float32)
+    for t in range(T - 1):  # every cached key was rotated at its own position
+        oracle.rope_interleaved(scratch, k[t], hd, t, cr, ci)
+    xb, _, _ = gpu_decode(gla_ctx, q, k, v, nh, nkv, hd, T)
+    assert_close(xb, oracle.decode_f32(q, k, v, nh, nkv, hd, T), TOL_F32, "C2")
+
+
+def test_c4_long_context_full_size(gla_ctx, oracle):
+    # Qwen2.5-7B shape, context 131072, FP16 cache
+    nh, nkv, hd, T = 28, 4, 128, 131072
+    q, k, v = inputs.decode_case(42, nh, nkv, hd, T)
+    k16, v16 = inputs.to_f16_bits(k), inputs.to_f16_bits(v)
+    del k, v
+    xb, _, _ = gpu_decode(gla_ctx, q, k16.view(np.float16).astype(np.float32),
+                          v16.view(np.float16).astype(np.float32), nh, nkv, hd, T, f16=True)
+    assert_close(xb, oracle.decode_f16(q, k16, v16, nh, nkv, hd, T), TOL_F16, "C4")
+
+
+def test_rope_append_matches_oracle(gla_ctx, oracle):
+    import os
+
+    torch = _torch()
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "attention_golden.npz"))
+    for name in ("rope_llama3_theta5e5_pos123", "rope_neox_theta1e6_pos77"):
+        seed, nh, nkv, hd, pos, style = (int(x) for x in g[f"{name}/meta"])
+        theta = float(g[f"{name}/theta"])
+        qd, kd = dev(g[f"{name}/q_in"]), dev(g[f"{name}/k_in"])
+        rng = np.random.Generator(np.random.PCG64(seed + 1))
+        vin = rng.standard_normal(nkv * hd, dtype=np.float32)
+        vd = dev(vin)
+        kc = torch.zeros(pos + 1, nkv * hd, device="cuda")
+        vc = torch.zeros_like(kc)
+        ph = torch.tensor([pos], dtype=torch.int32, device="cuda")
+        gla_ctx.rope_append(qd, kd, vd, kc, vc, nh, nkv, hd, ph, theta, style)
+        assert gla_ctx.device_status() == 0
+        np.testing.assert_allclose(qd.cpu().numpy(), g[f"{name}/q_out"], rtol=0, atol=2e-6)
+        np.testing.assert_allclose(kd.cpu().numpy(), g[f"{name}/k_out"], rtol=0, atol=2e-6)
+        np.testing.assert_array_equal(kc[pos].cpu().numpy(), kd.cpu().numpy())
+        np.testing.assert_array_equal(vc[pos].cpu().numpy(), vin)
+        assert float(kc[:pos].abs().sum()) == 0.0
