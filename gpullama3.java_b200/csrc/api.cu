@@ -12,7 +12,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/gpullama_attn.h"
+#include "gpullama_attn.h"
 #include "gla_common.cuh"
 #include "gla_internal.h"
 #include "gla_comm.h"
@@ -378,7 +378,7 @@ int32_t gla_reserve(gla_ctx* ctx, int32_t max_batch, int32_t max_kv_heads, int32
   const int group = std::max(1, max_heads / max_kv_heads);
   DeviceGuard dg(ctx->device);
   const size_t part = (size_t)(ctx->dev.sms + (size_t)max_batch * max_kv_heads) * group *
-                      (max_head_dim + 2);
+                      (max_head_dim + 4);
   return ensure_workspace(ctx, part, (size_t)max_batch * max_kv_heads);
 }
 

@@ -5,7 +5,7 @@
 #include <cstring>
 #include <mutex>
 
-#include "../../include/gpullama_attn.h"
+#include "gpullama_attn.h"
 #include "gla_comm.h"
 
 namespace gla {

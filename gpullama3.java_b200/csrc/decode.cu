@@ -1,5 +1,7 @@
 // decode.cu - launch planning and template instantiation of the split-KV
 // decode kernel (decode_kernel.cuh).
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cmath>
 #include <mutex>
@@ -11,18 +13,17 @@ namespace gla {
 
 namespace {
 
-constexpr int kNWf32 = 8;  // consumer warps, FP32 cache
-constexpr int kNWf16 = 4;  // consumer warps, FP16 cache
+constexpr int kNW = 4;  // consumer warps (both consumers)
+constexpr int kTileMax = 64;
 constexpr int kMaxStages = 8;
 
 size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 
-int tile_max_for(int dtype, int hd) {
-  if (dtype == GLA_DTYPE_F16) return 16 * kNWf16;
-  return hd <= 64 ? 64 : 32;
-}
+// LOADER 0 (tiled TMA) for one sequence whose base pointer the host knows;
+// LOADER 1 (cp.async) when the per-sequence bases live in device memory.
+int loader_for(const DecodeRequest& r) { return r.k_ptrs ? 1 : 0; }
 
-int row_bytes_for(int dtype, int hd) { return dtype == GLA_DTYPE_F16 ? (hd + 8) * 2 : hd * 4; }
+int esize_for(int dtype) { return dtype == GLA_DTYPE_F32 ? 4 : 2; }
 
 int group_cap_for(int dtype, int group) {
   if (dtype == GLA_DTYPE_F16) return kMaxGroup;
@@ -31,51 +32,126 @@ int group_cap_for(int dtype, int group) {
 
 // Shared memory layout for a given tile/stage count.
 struct Layout {
-  int32_t off_bars, off_seq, off_pbuf, off_merge, off_flags;
+  int32_t off_bars, off_seq, off_q, off_pbuf, off_merge, off_comb, off_flags;
   size_t total;
 };
 
-Layout layout_for(int dtype, int hd, int group, int tile, int stages, int batch) {
-  const int nw = dtype == GLA_DTYPE_F16 ? kNWf16 : kNWf32;
+Layout layout_for(int dtype, int hd, int group, int tile, int stages, int batch, int grid) {
   Layout L;
-  size_t off = (size_t)stages * 2 * tile * row_bytes_for(dtype, hd);
+  size_t off = (size_t)stages * 2 * tile * hd * esize_for(dtype);
   L.off_bars = (int32_t)align16(off);
   off = L.off_bars + (size_t)stages * 2 * sizeof(uint64_t);
   L.off_seq = (int32_t)align16(off);
   off = L.off_seq + (size_t)(3 * batch + 1) * sizeof(int32_t);
+  L.off_q = (int32_t)align16(off);
+  off = L.off_q + (size_t)kMaxGroup * hd * sizeof(float);
   L.off_pbuf = (int32_t)align16(off);
-  off = L.off_pbuf + (dtype == GLA_DTYPE_F16 ? 0 : (size_t)nw * 64 * sizeof(float));
+  off = L.off_pbuf + (dtype == GLA_DTYPE_F16 ? 0 : (size_t)kNW * 16 * 8 * sizeof(float));
   L.off_merge = (int32_t)align16(off);
-  off = L.off_merge + (size_t)nw * group_cap_for(dtype, group) * (hd + 2) * sizeof(float);
+  off = L.off_merge + (size_t)kNW * group_cap_for(dtype, group) * (hd + 2) * sizeof(float);
+  L.off_comb = (int32_t)align16(off);
+  off = L.off_comb + (size_t)(2 * grid + 2) * kMaxGroup * sizeof(float);
   L.off_flags = (int32_t)align16(off);
-  L.total = L.off_flags + 16;
+  L.total = L.off_flags + 16 + 1024;  // + slack to 1024-align the stage ring
   return L;
 }
 
 template <class Kern>
 void ensure_smem_attr(Kern kern, size_t bytes) {
-  // cudaFuncSetAttribute is per device; setting it on every launch is cheap
-  // compared with a failed launch, but skip it below the default 48 KB.
-  if (bytes > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (bytes > 48 * 1024)
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
-template <int HD, int NW, class C>
+template <int HD, class C, int LOADER>
 cudaError_t launch_impl(const DecodeArgs& a, const DecodePlan& p, cudaStream_t st) {
-  auto kern = decode_kernel<HD, NW, C>;
+  auto kern = decode_kernel<HD, C, LOADER>;
   ensure_smem_attr(kern, p.smem);
-  kern<<<p.grid, p.threads, p.smem, st>>>(a);
-  return cudaGetLastError();
+  // programmatic dependent launch: this grid's CTAs may start (prologue
+  // only; the kernel waits on griddepcontrol before touching memory) while
+  // the previous kernel on the stream drains
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(p.threads);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
-template <int HD>
+template <int HD, int LOADER>
 cudaError_t launch_f32(const DecodeArgs& a, const DecodePlan& p, cudaStream_t st) {
-  const int gc = group_cap_for(GLA_DTYPE_F32, a.group);
-  switch (gc) {
-    case 1: return launch_impl<HD, kNWf32, F32Consumer<HD, 1, kNWf32>>(a, p, st);
-    case 2: return launch_impl<HD, kNWf32, F32Consumer<HD, 2, kNWf32>>(a, p, st);
-    case 4: return launch_impl<HD, kNWf32, F32Consumer<HD, 4, kNWf32>>(a, p, st);
-    default: return launch_impl<HD, kNWf32, F32Consumer<HD, 8, kNWf32>>(a, p, st);
+  switch (group_cap_for(GLA_DTYPE_F32, a.group)) {
+    case 1: return launch_impl<HD, F32Consumer<HD, 1>, LOADER>(a, p, st);
+    case 2: return launch_impl<HD, F32Consumer<HD, 2>, LOADER>(a, p, st);
+    case 4: return launch_impl<HD, F32Consumer<HD, 4>, LOADER>(a, p, st);
+    default: return launch_impl<HD, F32Consumer<HD, 8>, LOADER>(a, p, st);
   }
+}
+
+template <int LOADER>
+cudaError_t launch_any(int dtype, int hd, const DecodeArgs& a, const DecodePlan& p,
+                       cudaStream_t st) {
+  if (dtype == GLA_DTYPE_F32) {
+    switch (hd) {
+      case 64: return launch_f32<64, LOADER>(a, p, st);
+      case 96: return launch_f32<96, LOADER>(a, p, st);
+      default: return launch_f32<128, LOADER>(a, p, st);
+    }
+  }
+  switch (hd) {
+    case 64: return launch_impl<64, F16Consumer<64>, LOADER>(a, p, st);
+    case 96: return launch_impl<96, F16Consumer<96>, LOADER>(a, p, st);
+    default: return launch_impl<128, F16Consumer<128>, LOADER>(a, p, st);
+  }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// dependency on libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2D map over a cache [rows][kv_stride] with boxes of one column block x tile
+// rows, swizzled like TileLayout (128B for 128-byte block rows, 64B for 64).
+bool encode_kv_map(CUtensorMap* map, const void* base, int dtype, int hd, int64_t kv_stride,
+                   int64_t rows, int tile, std::string* err) {
+  auto fn = encode_fn();
+  if (!fn) {
+    *err = "cuTensorMapEncodeTiled unavailable";
+    return false;
+  }
+  const int esize = esize_for(dtype);
+  const int cw = dtype == GLA_DTYPE_F32 ? 32 : (hd % 64 == 0 ? 64 : 32);
+  const CUtensorMapSwizzle swz =
+      cw * esize == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  cuuint64_t dims[2] = {(cuuint64_t)kv_stride, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(kv_stride * esize)};
+  cuuint32_t box[2] = {(cuuint32_t)cw, (cuuint32_t)tile};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype == GLA_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                  2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *err = "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")";
+    return false;
+  }
+  return true;
 }
 
 }  // namespace
@@ -97,7 +173,7 @@ int plan_decode(const DecodeRequest& r, const DeviceInfo& dev, DecodePlan* p, st
   }
   // Tile: largest tile that still gives every SM at least two tiles.
   const int64_t rows = std::max<int64_t>(1, r.max_n_pos);
-  int tile = tile_max_for(r.dtype, hd);
+  int tile = kTileMax;
   auto tiles_at = [&](int t) { return (int64_t)r.batch * r.n_kv * ((rows + t - 1) / t); };
   while (tile > 16 && tiles_at(tile) < 2 * (int64_t)dev.sms) tile >>= 1;
   const int64_t W = tiles_at(tile);
@@ -111,10 +187,10 @@ int plan_decode(const DecodeRequest& r, const DeviceInfo& dev, DecodePlan* p, st
   grid = std::max(grid, 1);
   // Stages: as many as fit (the ring is the only large smem consumer).
   int stages = kMaxStages;
-  Layout L = layout_for(r.dtype, hd, group, tile, stages, r.batch);
+  Layout L = layout_for(r.dtype, hd, group, tile, stages, r.batch, grid);
   while (stages > 2 && L.total > (size_t)dev.smem_optin) {
     --stages;
-    L = layout_for(r.dtype, hd, group, tile, stages, r.batch);
+    L = layout_for(r.dtype, hd, group, tile, stages, r.batch, grid);
   }
   if (L.total > (size_t)dev.smem_optin) {
     *err = "shared memory layout does not fit";
@@ -123,9 +199,9 @@ int plan_decode(const DecodeRequest& r, const DeviceInfo& dev, DecodePlan* p, st
   p->tile = tile;
   p->stages = stages;
   p->grid = grid;
-  p->threads = ((r.dtype == GLA_DTYPE_F16 ? kNWf16 : kNWf32) + 1) * 32;
+  p->threads = (kNW + 1) * 32;
   p->smem = L.total;
-  p->part_floats = (size_t)(grid + r.batch * r.n_kv) * group * (hd + 2);
+  p->part_floats = (size_t)(grid + r.batch * r.n_kv) * group * (hd + 4);
   p->counters = (size_t)r.batch * r.n_kv;
   return GLA_OK;
 }
@@ -134,8 +210,14 @@ int launch_decode(const DecodeRequest& r, const DecodePlan& p, float* ws_part, i
                   int32_t* status, cudaStream_t stream, std::string* err) {
   const int hd = r.head_dim;
   const int group = r.n_heads / r.n_kv;
-  Layout L = layout_for(r.dtype, hd, group, p.tile, p.stages, r.batch);
+  const int loader = loader_for(r);
+  Layout L = layout_for(r.dtype, hd, group, p.tile, p.stages, r.batch, p.grid);
   DecodeArgs a{};
+  if (loader == 0) {
+    if (!encode_kv_map(&a.tmap_k, r.k, r.dtype, hd, r.kv_stride, r.n_pos_cap, p.tile, err) ||
+        !encode_kv_map(&a.tmap_v, r.v, r.dtype, hd, r.kv_stride, r.n_pos_cap, p.tile, err))
+      return GLA_ERR_INVALID_ARG;
+  }
   a.q = r.q;
   a.k = r.k;
   a.v = r.v;
@@ -158,27 +240,16 @@ int launch_decode(const DecodeRequest& r, const DecodePlan& p, float* ws_part, i
   a.ws_part = ws_part;
   a.ws_counter = ws_counter;
   a.status = status;
-  a.row_bytes = row_bytes_for(r.dtype, hd);
-  a.stage_bytes = 2 * p.tile * a.row_bytes;
+  a.stage_bytes = 2 * p.tile * hd * esize_for(r.dtype);
   a.off_bars = L.off_bars;
   a.off_seq = L.off_seq;
   a.off_pbuf = L.off_pbuf;
+  a.off_q = L.off_q;
   a.off_merge = L.off_merge;
+  a.off_comb = L.off_comb;
   a.off_flags = L.off_flags;
-  cudaError_t rc;
-  if (r.dtype == GLA_DTYPE_F32) {
-    switch (hd) {
-      case 64: rc = launch_f32<64>(a, p, stream); break;
-      case 96: rc = launch_f32<96>(a, p, stream); break;
-      default: rc = launch_f32<128>(a, p, stream); break;
-    }
-  } else {
-    switch (hd) {
-      case 64: rc = launch_impl<64, kNWf16, F16Consumer<64, kNWf16>>(a, p, stream); break;
-      case 96: rc = launch_impl<96, kNWf16, F16Consumer<96, kNWf16>>(a, p, stream); break;
-      default: rc = launch_impl<128, kNWf16, F16Consumer<128, kNWf16>>(a, p, stream); break;
-    }
-  }
+  cudaError_t rc = loader == 0 ? launch_any<0>(r.dtype, hd, a, p, stream)
+                                : launch_any<1>(r.dtype, hd, a, p, stream);
   if (rc != cudaSuccess) {
     *err = std::string("decode launch failed: ") + cudaGetErrorString(rc);
     return GLA_ERR_CUDA;

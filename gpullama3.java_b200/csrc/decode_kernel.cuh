@@ -10,15 +10,20 @@
 //  * The tiles of all (sequence, kv head) segments are dealt to the CTAs in
 //    contiguous near-equal ranges (gla_common.cuh), so every SM streams the
 //    same number of KV bytes whatever the sequence lengths.
-//  * Warp NW is the producer: per tile it issues one bulk TMA copy
-//    (cp.async.bulk) per K row and per V row into a ring of `stages` shared
-//    memory stages guarded by full/empty mbarriers.  Rows of one kv head are
-//    head_dim contiguous elements, so each copy is a 128-512 byte burst and
-//    HBM sees long coalesced reads.
-//  * Warps 0..NW-1 consume every stage together; each owns a fixed slice of
-//    the tile's rows and keeps its own online-softmax state (m, l, o) for all
-//    G q heads of the group, so all heads of a group share one K/V tile read
-//    and no CTA-wide barrier is needed per tile.
+//  * Warp NW is the producer.  It fills a ring of `stages` shared-memory
+//    stages guarded by full/empty mbarriers, one K tile and one V tile
+//    (`tile` rows of one kv head) per stage:
+//      LOADER 0 (single sequence): tiled TMA, one cp.async.bulk.tensor.2d per
+//        tensor and column block through a 2D tensor map [rows][kv_stride];
+//        FP16 tiles land 128B/64B-swizzled so ldmatrix is conflict-free;
+//        rows past the cache end are zero-filled by the TMA unit.
+//      LOADER 1 (batched, per-sequence pointers read on the device): 16-byte
+//        cp.async into the same swizzled layout, completion via
+//        cp.async.mbarrier.arrive.
+//  * Warps 0..NW-1 consume every stage together; each owns 16 rows of the
+//    tile and keeps its own online-softmax state (m, l, o) for all G q heads
+//    of the group, so all heads of a group share one K/V tile read and no
+//    CTA-wide barrier is needed per tile.
 //  * At the end of a segment piece the warps merge their states in shared
 //    memory.  A segment held by one CTA is written straight to xb; otherwise
 //    each CTA stores its piece to a workspace slot and the last CTA to finish
@@ -36,6 +41,8 @@
 namespace gla {
 
 struct DecodeArgs {
+  CUtensorMap tmap_k;          // LOADER 0: [rows][kv_stride] box (col_block, tile)
+  CUtensorMap tmap_v;
   const float* q;              // [B][n_heads][HD]
   const void* k;               // layer base (single sequence) or nullptr
   const void* v;
@@ -56,56 +63,77 @@ struct DecodeArgs {
   float q_scale;               // scale * log2(e)
   float* out;                  // xb [B][n_heads][HD] or records [B][n_heads][HD+2]
   int32_t record_mode;
-  float* ws_part;              // workspace slots [P + B*n_kv][G][HD+2]
+  float* ws_part;              // workspace slots [P + B*n_kv][G][HD+4] (o, m, l, pad)
   int32_t* ws_counter;         // [B*n_kv], zero between calls
   int32_t* status;             // device status word
   // shared memory layout (bytes)
-  int32_t row_bytes;           // smem bytes per cached row (incl. padding)
-  int32_t stage_bytes;         // 2 * tile * row_bytes
+  int32_t stage_bytes;         // 2 * tile * head_dim * element size
   int32_t off_bars;
   int32_t off_seq;
   int32_t off_pbuf;
+  int32_t off_q;               // the group's q vectors [kMaxGroup][HD]
   int32_t off_merge;
+  int32_t off_comb;            // combine scratch: m/l per (piece, head), M/L per head
   int32_t off_flags;
 };
+
+// Floats per head in a workspace piece slot: o[HD], m, l, 2 pad (16-byte rows).
+template <int HD>
+constexpr int slot_head_floats() { return HD + 4; }
 
 constexpr float kLn2 = 0.69314718055994530942f;
 
 // ---------------------------------------------------------------------------
-// FP32 cache consumer: 16 lanes per row in phase A (q.k), all 32 lanes across
-// head_dim in phase B (p.v).
+// Tile layout in shared memory (both loaders write it, both consumers read
+// it): each tensor tile is split into column blocks of kCW elements; block cb
+// holds [tile][kCW] rows of kRowB bytes with the TMA swizzle applied: the
+// 16-byte chunk c of row r sits at chunk c ^ (r & 7) for 128-byte rows
+// (SWIZZLE_128B) and c ^ ((r >> 1) & 3) for 64-byte rows (SWIZZLE_64B).
+// Reading 8 consecutive rows at one logical chunk (ldmatrix, or one row per
+// lane) therefore touches 8 different bank groups.
 // ---------------------------------------------------------------------------
-template <int HD, int GT, int NW>
-struct F32Consumer {
-  static constexpr int kVecA = (HD % 64 == 0) ? 4 : 2;   // floats per phase-A load
-  static constexpr int kChunksA = HD / 16 / kVecA;       // loads per lane per row
-  static constexpr int kVB = HD / 32;                    // floats per lane in phase B
-  static constexpr int kTileMax = (HD <= 64) ? 64 : 32;
-  static constexpr int kMaxPass = kTileMax / NW / 2;
-  static constexpr int kMergeG = GT;
-  static constexpr int kElemBytes = 4;
-  static constexpr int kRowBytes = HD * 4;
-  static constexpr int kPbufFloats = 64;  // per warp: <= 8 rows x 8 heads
-  static_assert(HD % 32 == 0 || HD == 96, "head_dim");
+template <int ESIZE, int HD>
+struct TileLayout {
+  static constexpr int kCW = (ESIZE == 4) ? 32 : ((HD % 64 == 0) ? 64 : 32);
+  static constexpr int kRowB = kCW * ESIZE;  // 128 or 64
+  static constexpr int kBlocks = HD / kCW;
+  static_assert(HD % kCW == 0, "head_dim must be a multiple of the column block");
+  // byte offset of the 16-byte chunk holding (row, col); col % (16/ESIZE) == 0
+  __device__ __forceinline__ static int chunk_off(int tile, int row, int col) {
+    const int cb = col / kCW;
+    const int c = ((col % kCW) * ESIZE) >> 4;
+    const int sw = (kRowB == 128) ? (row & 7) : ((row >> 1) & 3);
+    return cb * tile * kRowB + row * kRowB + ((c ^ sw) << 4);
+  }
+};
 
-  float qreg[GT][HD / 16];
-  float m[GT], l[GT];
+// ---------------------------------------------------------------------------
+// FP32 cache consumer (CUDA-core FMA; an FP32 cache delivers at most G/2 FLOP
+// per byte).  Each warp owns 16 rows of a tile.
+//   phase A (q.k): lane = (row, half of head_dim); the lane streams its
+//     row's K chunks and multiplies them with the G q vectors, broadcast from
+//     shared memory; one shuffle joins the two halves.
+//   online softmax: one 16-row max per head per tile.
+//   phase B (p.v): lane = 1/32 of head_dim; rows are accumulated in turn.
+// ---------------------------------------------------------------------------
+template <int HD, int GT>
+struct F32Consumer {
+  using TL = TileLayout<4, HD>;
+  static constexpr int kElemBytes = 4;
+  static constexpr int kNW = 4;
+  static constexpr int kTileMax = 16 * kNW;
+  static constexpr int kMergeG = GT;
+  static constexpr int kPbufFloats = 16 * 8;  // per warp: 16 rows x 8 heads
+  static constexpr int kChunks = HD / 4;      // float4 chunks per row
+  static constexpr int kHalf = kChunks / 2;   // phase A chunks per lane
+  static constexpr int kVB = HD / 32;         // phase B floats per lane
+
+  float m[GT], l[GT];  // m: warp-uniform; l: per-lane part (lanes 0-15 own rows)
   float o[GT][kVB];
 
-  __device__ __forceinline__ void begin(const DecodeArgs& a, int b, int g, int lane) {
-    const int j = lane & 15;
-    const float* qb = a.q + ((int64_t)b * a.n_heads + (int64_t)g * a.group) * HD;
+  __device__ __forceinline__ void begin(const DecodeArgs&, const float*, int) {
 #pragma unroll
     for (int h = 0; h < GT; ++h) {
-#pragma unroll
-      for (int c = 0; c < kChunksA; ++c) {
-#pragma unroll
-        for (int e = 0; e < kVecA; ++e) {
-          float x = 0.f;
-          if (h < a.group) x = qb[h * HD + (c * 16 + j) * kVecA + e] * a.q_scale;
-          qreg[h][c * kVecA + e] = x;
-        }
-      }
       m[h] = -INFINITY;
       l[h] = 0.f;
 #pragma unroll
@@ -114,102 +142,78 @@ struct F32Consumer {
   }
 
   __device__ __forceinline__ void consume(const DecodeArgs& a, const char* stage, int rows,
-                                          float* pbuf_w, int w, int lane) {
-    const float* Ks = reinterpret_cast<const float*>(stage);
-    const float* Vs = reinterpret_cast<const float*>(stage + a.tile * kRowBytes);
-    const int rpw = a.tile / NW;
-    const int npass = rpw >> 1;
-    const int half = lane >> 4, j = lane & 15;
-    const int row_base = w * rpw;
-    float s[kMaxPass][GT];
+                                          float* pbuf_w, const float* qs, int w, int lane) {
+    const int rb = w * 16;
+    if (rb >= rows) return;
+    const int rl = lane & 15, half = lane >> 4;
+    const int row = rb + rl;
+    const char* Ks = stage;
+    const char* Vs = stage + a.tile * HD * 4;
+    float acc[GT];
 #pragma unroll
-    for (int pp = 0; pp < kMaxPass; ++pp) {
-      if (pp < npass) {
-        const int row = row_base + 2 * pp + half;
-        const float* kr = Ks + row * HD;
-        float acc[GT];
+    for (int h = 0; h < GT; ++h) acc[h] = 0.f;
 #pragma unroll
-        for (int h = 0; h < GT; ++h) acc[h] = 0.f;
+    for (int i = 0; i < kHalf; ++i) {
+      const int c = half * kHalf + i;
+      const float4 k4 = *reinterpret_cast<const float4*>(Ks + TL::chunk_off(a.tile, row, c * 4));
 #pragma unroll
-        for (int c = 0; c < kChunksA; ++c) {
-          float kv[kVecA];
-          if constexpr (kVecA == 4) {
-            float4 t = *reinterpret_cast<const float4*>(kr + (c * 16 + j) * 4);
-            kv[0] = t.x; kv[1] = t.y; kv[2] = t.z; kv[3] = t.w;
-          } else {
-            float2 t = *reinterpret_cast<const float2*>(kr + (c * 16 + j) * 2);
-            kv[0] = t.x; kv[1] = t.y;
-          }
-#pragma unroll
-          for (int h = 0; h < GT; ++h)
-#pragma unroll
-            for (int e = 0; e < kVecA; ++e) acc[h] = fmaf(qreg[h][c * kVecA + e], kv[e], acc[h]);
-        }
-#pragma unroll
-        for (int off = 8; off >= 1; off >>= 1)
-#pragma unroll
-          for (int h = 0; h < GT; ++h) acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], off);
-        const bool valid = row < rows;
-#pragma unroll
-        for (int h = 0; h < GT; ++h) s[pp][h] = valid ? acc[h] : -INFINITY;
-      } else {
-#pragma unroll
-        for (int h = 0; h < GT; ++h) s[pp][h] = -INFINITY;
+      for (int h = 0; h < GT; ++h) {
+        const float4 q4 = *reinterpret_cast<const float4*>(qs + h * HD + c * 4);
+        acc[h] = fmaf(q4.x, k4.x, acc[h]);
+        acc[h] = fmaf(q4.y, k4.y, acc[h]);
+        acc[h] = fmaf(q4.z, k4.z, acc[h]);
+        acc[h] = fmaf(q4.w, k4.w, acc[h]);
       }
     }
-    // online softmax over this warp's rows of the tile
+    const bool valid = row < rows;
+    float p[GT];
 #pragma unroll
     for (int h = 0; h < GT; ++h) {
-      float mt = s[0][h];
+      const float sc = acc[h] + __shfl_xor_sync(0xffffffffu, acc[h], 16);
+      const float s = valid ? sc : -INFINITY;
+      float mt = s;
 #pragma unroll
-      for (int pp = 1; pp < kMaxPass; ++pp) mt = fmaxf(mt, s[pp][h]);
-      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
-      const float mn = fmaxf(m[h], mt);
-      const bool none = (mn == -INFINITY);
-      const float alpha = none ? 1.f : fast_exp2(m[h] - mn);
-      float psum = 0.f;
-#pragma unroll
-      for (int pp = 0; pp < kMaxPass; ++pp) {
-        const float p = none ? 0.f : fast_exp2(s[pp][h] - mn);
-        s[pp][h] = p;
-        psum += p;
-      }
-      psum += __shfl_xor_sync(0xffffffffu, psum, 16);
-      l[h] = l[h] * alpha + psum;
+      for (int off = 8; off >= 1; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+      const float mn = fmaxf(m[h], mt);  // finite: row rb is valid
+      const float alpha = fast_exp2(m[h] - mn);
+      p[h] = fast_exp2(s - mn);
+      l[h] = l[h] * alpha + (half == 0 ? p[h] : 0.f);
       m[h] = mn;
 #pragma unroll
       for (int e = 0; e < kVB; ++e) o[h][e] *= alpha;
     }
-    if (j == 0) {
+    if (half == 0) {
+      float* pr = pbuf_w + rl * 8;
 #pragma unroll
-      for (int pp = 0; pp < kMaxPass; ++pp) {
-        if (pp < npass) {
-#pragma unroll
-          for (int h = 0; h < GT; ++h) pbuf_w[(2 * pp + half) * 8 + h] = s[pp][h];
-        }
-      }
+      for (int h = 0; h < GT; ++h) pr[h] = p[h];
     }
     __syncwarp();
-    const int nrows = min(rpw, rows - row_base);
+    const int nrows = min(16, rows - rb);
     for (int r = 0; r < nrows; ++r) {
-      const float* vr = Vs + (row_base + r) * HD + lane * kVB;
+      const int vrow = rb + r;
       float vv[kVB];
       if constexpr (kVB == 4) {
-        float4 t = *reinterpret_cast<const float4*>(vr);
+        const float4 t = *reinterpret_cast<const float4*>(Vs + TL::chunk_off(a.tile, vrow, lane * 4));
         vv[0] = t.x; vv[1] = t.y; vv[2] = t.z; vv[3] = t.w;
       } else if constexpr (kVB == 2) {
-        float2 t = *reinterpret_cast<const float2*>(vr);
+        const int d = lane * 2;
+        const float2 t = *reinterpret_cast<const float2*>(
+            Vs + TL::chunk_off(a.tile, vrow, d & ~3) + (d & 3) * 4);
         vv[0] = t.x; vv[1] = t.y;
       } else {
 #pragma unroll
-        for (int e = 0; e < kVB; ++e) vv[e] = vr[e];
+        for (int e = 0; e < kVB; ++e) {
+          const int d = lane * kVB + e;
+          vv[e] = *reinterpret_cast<const float*>(Vs + TL::chunk_off(a.tile, vrow, d & ~3) +
+                                                  (d & 3) * 4);
+        }
       }
-      float pr[GT];
       const float* prow = pbuf_w + r * 8;
+      float pr[GT];
       if constexpr (GT >= 4) {
 #pragma unroll
         for (int h4 = 0; h4 < GT; h4 += 4) {
-          float4 t = *reinterpret_cast<const float4*>(prow + h4);
+          const float4 t = *reinterpret_cast<const float4*>(prow + h4);
           pr[h4] = t.x; pr[h4 + 1] = t.y; pr[h4 + 2] = t.z; pr[h4 + 3] = t.w;
         }
       } else {
@@ -224,17 +228,20 @@ struct F32Consumer {
     __syncwarp();
   }
 
-  // Writes this warp's (m, l, o) for q heads h < group into merge_w[h][HD+2].
+  // Writes this warp's (o, m, l) for q heads h < group into merge_w[h][HD+2].
   __device__ __forceinline__ void to_merge(const DecodeArgs& a, float* merge_w, int lane) {
 #pragma unroll
     for (int h = 0; h < GT; ++h) {
+      float lt = l[h];
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, off);
       if (h < a.group) {
         float* mh = merge_w + h * (HD + 2);
 #pragma unroll
         for (int e = 0; e < kVB; ++e) mh[lane * kVB + e] = o[h][e];
         if (lane == 0) {
           mh[HD] = m[h];
-          mh[HD + 1] = l[h];
+          mh[HD + 1] = lt;
         }
       }
     }
@@ -287,13 +294,13 @@ __device__ __forceinline__ uint32_t mask_pair(uint32_t r, int p0, int nvalid) {
   return r & keep;
 }
 
-template <int HD, int NW>
+template <int HD>
 struct F16Consumer {
-  static constexpr int kRS = HD + 8;             // smem row stride in halves (16 B pad)
-  static constexpr int kRowBytes = kRS * 2;
+  using TL = TileLayout<2, HD>;
   static constexpr int kElemBytes = 2;
+  static constexpr int kNW = 4;
   static constexpr int kPbufFloats = 0;
-  static constexpr int kTileMax = 16 * NW;
+  static constexpr int kTileMax = 16 * kNW;
   static constexpr int kMergeG = kMaxGroup;
   static constexpr int kKS = HD / 16;            // k-steps of q.k
   static constexpr int kNT = HD / 8;             // n-tiles of p.v
@@ -303,20 +310,21 @@ struct F16Consumer {
   float m_run, l_run;
   float oacc[kNT][4];
 
-  __device__ __forceinline__ void begin(const DecodeArgs& a, int b, int g, int lane) {
+  __device__ __forceinline__ static uint32_t chunk(uint32_t base, int tile, int row, int col) {
+    return base + (uint32_t)TL::chunk_off(tile, row, col);
+  }
+
+  // qs: the group's pre-scaled q vectors [kMaxGroup][HD] in shared memory
+  // (rows >= group are zero).
+  __device__ __forceinline__ void begin(const DecodeArgs&, const float* qs, int lane) {
     const int gid = lane >> 2, tig = lane & 3;
-    const float* qh = a.q + ((int64_t)b * a.n_heads + (int64_t)g * a.group + gid) * HD;
-    const bool live = gid < a.group;
+    const float* qh = qs + gid * HD;
 #pragma unroll
     for (int kk = 0; kk < kKS; ++kk) {
       const int c0 = kk * 16 + 2 * tig, c1 = c0 + 8;
-      float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
-      if (live) {
-        float2 u = *reinterpret_cast<const float2*>(qh + c0);
-        float2 w = *reinterpret_cast<const float2*>(qh + c1);
-        x0 = u.x * a.q_scale; x1 = u.y * a.q_scale;
-        x2 = w.x * a.q_scale; x3 = w.y * a.q_scale;
-      }
+      const float2 u = *reinterpret_cast<const float2*>(qh + c0);
+      const float2 w = *reinterpret_cast<const float2*>(qh + c1);
+      const float x0 = u.x, x1 = u.y, x2 = w.x, x3 = w.y;
       __half h0, l0, h1, l1, h2, l2, h3, l3;
       split_half(x0, h0, l0); split_half(x1, h1, l1);
       split_half(x2, h2, l2); split_half(x3, h3, l3);
@@ -334,13 +342,14 @@ struct F16Consumer {
   }
 
   __device__ __forceinline__ void consume(const DecodeArgs& a, const char* stage, int rows,
-                                          float* /*pbuf_w*/, int w, int lane) {
+                                          float* /*pbuf_w*/, const float* /*qs*/, int w,
+                                          int lane) {
     const int rb = w * 16;
     if (rb >= rows) return;
     const int nvalid = min(16, rows - rb);
     const int tig = lane & 3;
-    const uint32_t kbase = smem_u32(stage) + (uint32_t)(rb * kRowBytes);
-    const uint32_t vbase = kbase + (uint32_t)(a.tile * kRowBytes);
+    const uint32_t kbase = smem_u32(stage);
+    const uint32_t vbase = kbase + (uint32_t)(a.tile * HD * 2);
     float sacc[2][4];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
@@ -350,8 +359,7 @@ struct F16Consumer {
     for (int kk = 0; kk < kKS; kk += 2) {
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        const uint32_t addr =
-            kbase + (uint32_t)(((nt * 8 + (lane & 7)) * kRS + kk * 16 + (lane >> 3) * 8) * 2);
+        const uint32_t addr = chunk(kbase, a.tile, rb + nt * 8 + (lane & 7), kk * 16 + (lane >> 3) * 8);
         uint32_t r0, r1, r2, r3;
         ldsm_x4(addr, r0, r1, r2, r3);
         mma_16816(sacc[nt], qa[kk], r0, r1);
@@ -402,7 +410,7 @@ struct F16Consumer {
 #pragma unroll
     for (int nt = 0; nt < kNT; nt += 2) {
       const uint32_t addr =
-          vbase + (uint32_t)((((lane & 7) + ((lane >> 3) & 1) * 8) * kRS + (nt + (lane >> 4)) * 8) * 2);
+          chunk(vbase, a.tile, rb + (lane & 7) + ((lane >> 3) & 1) * 8, (nt + (lane >> 4)) * 8);
       uint32_t r0, r1, r2, r3;
       ldsm_x4_t(addr, r0, r1, r2, r3);
       if (partial) {
@@ -455,14 +463,41 @@ __device__ __forceinline__ void write_final(const DecodeArgs& a, int b, int hq, 
   }
 }
 
+template <int HD>
+__device__ __forceinline__ void write_final4(const DecodeArgs& a, int b, int hq, int d, float4 O,
+                                             float M, float L) {
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  if (a.record_mode) {
+    write_final<HD>(a, b, hq, d, O.x, M, L);
+    write_final<HD>(a, b, hq, d + 1, O.y, M, L);
+    write_final<HD>(a, b, hq, d + 2, O.z, M, L);
+    write_final<HD>(a, b, hq, d + 3, O.w, M, L);
+  } else {
+    const int64_t row = (int64_t)b * a.n_heads + hq;
+    float4 r;
+    r.x = L > 0.f ? O.x / L : 0.f;
+    r.y = L > 0.f ? O.y / L : 0.f;
+    r.z = L > 0.f ? O.z / L : 0.f;
+    r.w = L > 0.f ? O.w / L : 0.f;
+    (void)inv;
+    *reinterpret_cast<float4*>(a.out + row * HD + d) = r;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
-template <int HD, int NW, class Consumer>
-__global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodeArgs a) {
-  extern __shared__ __align__(128) char smem[];
+template <int HD, class Consumer, int LOADER>
+__global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
+    decode_kernel(const __grid_constant__ DecodeArgs a) {
+  extern __shared__ __align__(1024) char smem_raw[];
+  // swizzled TMA tiles need 1024-byte aligned stages (the host adds the slack)
+  char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  constexpr int NW = Consumer::kNW;
   constexpr int kNCT = NW * 32;  // consumer threads
   constexpr int kMG = Consumer::kMergeG;
+  constexpr int esize = Consumer::kElemBytes;
+  using TL = TileLayout<esize, HD>;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int B = a.batch, n_kv = a.n_kv, G = a.group;
 
@@ -471,19 +506,29 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodeAr
   int32_t* seq_start = reinterpret_cast<int32_t*>(smem + a.off_seq);  // [B+1]
   int32_t* ntiles = seq_start + (B + 1);                              // [B]
   int32_t* npos = ntiles + B;                                         // [B]
+  float* qs = reinterpret_cast<float*>(smem + a.off_q);                // [kMaxGroup][HD]
   float* pbuf = reinterpret_cast<float*>(smem + a.off_pbuf);           // [NW][kPbufFloats]
   float* merge = reinterpret_cast<float*>(smem + a.off_merge);         // [NW][kMG][HD+2]
   volatile int* flags = reinterpret_cast<volatile int*>(smem + a.off_flags);  // [0]=abort [1]=last
 
   if (tid == 0) {
     for (int s = 0; s < a.stages; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], LOADER == 0 ? 1 : 32);
       mbar_init(&empty[s], NW);
     }
     flags[0] = 0;
     flags[1] = 0;
     fence_mbarrier_init();
   }
+  if (LOADER == 0 && warp == NW && lane == 0) {
+    prefetch_tmap(&a.tmap_k);
+    prefetch_tmap(&a.tmap_v);
+  }
+  // Programmatic dependent launch: everything above only touches shared
+  // memory and kernel parameters; nothing below may read memory a preceding
+  // kernel writes (n_pos, q, caches, the workspace) before that kernel is done.
+  pdl_wait();
+  pdl_launch_dependents();
   // per-sequence rows and tile prefix (warp 0 scans 32 sequences at a time)
   if (warp == 0) {
     int32_t carry = 0;
@@ -523,8 +568,6 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodeAr
     // ---------------- producer ----------------
     if (my_count > 0) {
       const uint64_t pol = l2_evict_first_policy();
-      constexpr int esize = Consumer::kElemBytes;
-      const uint32_t copy_bytes = HD * esize;
       TileRef tr = locate_tile(seq_start, ntiles, B, n_kv, my_lo);
       int cur_b = -1;
       const char* kb = nullptr;
@@ -533,29 +576,47 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodeAr
         const int st = i % a.stages;
         const uint32_t use = (uint32_t)(i / a.stages);
         if (!mbar_wait(&empty[st], (use & 1u) ^ 1u, flags, a.status)) break;
-        if (tr.b != cur_b) {
-          cur_b = tr.b;
-          kb = static_cast<const char*>(a.k_ptrs ? a.k_ptrs[cur_b] : a.k);
-          vb = static_cast<const char*>(a.v_ptrs ? a.v_ptrs[cur_b] : a.v);
-          // caller-supplied device pointers: a null or unaligned base would
-          // make the bulk copies fault, so refuse it and drain instead
-          if (kb == nullptr || vb == nullptr ||
-              ((reinterpret_cast<uintptr_t>(kb) | reinterpret_cast<uintptr_t>(vb)) & 15u)) {
-            atomicCAS(a.status, 0, GLA_ERR_ALIGNMENT);
-            flags[0] = 1;
-            break;
-          }
-        }
         const int row0 = tr.j * a.tile;
-        const int rows = min(a.tile, npos[tr.b] - row0);
-        if (lane == 0) mbar_arrive_expect_tx(&full[st], (uint32_t)rows * copy_bytes * 2u);
-        __syncwarp();
         char* ks = smem + (size_t)st * a.stage_bytes;
-        char* vs = ks + (size_t)a.tile * a.row_bytes;
-        for (int r = lane; r < rows; r += 32) {
-          const int64_t off = ((int64_t)(row0 + r) * a.kv_stride + (int64_t)tr.g * HD) * esize;
-          bulk_g2s(ks + (size_t)r * a.row_bytes, kb + off, copy_bytes, &full[st], pol);
-          bulk_g2s(vs + (size_t)r * a.row_bytes, vb + off, copy_bytes, &full[st], pol);
+        char* vs = ks + (size_t)a.tile * HD * esize;
+        if constexpr (LOADER == 0) {
+          // whole boxes, out-of-range rows zero-filled: the byte count is fixed
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * a.tile * HD * esize));
+#pragma unroll
+            for (int cb = 0; cb < TL::kBlocks; ++cb) {
+              const int x = tr.g * HD + cb * TL::kCW;
+              const size_t off = (size_t)cb * a.tile * TL::kRowB;
+              tma_load_2d(ks + off, &a.tmap_k, x, row0, &full[st], pol);
+              tma_load_2d(vs + off, &a.tmap_v, x, row0, &full[st], pol);
+            }
+          }
+          __syncwarp();
+        } else {
+          if (tr.b != cur_b) {
+            cur_b = tr.b;
+            kb = static_cast<const char*>(a.k_ptrs ? a.k_ptrs[cur_b] : a.k);
+            vb = static_cast<const char*>(a.v_ptrs ? a.v_ptrs[cur_b] : a.v);
+            // caller-supplied device pointers: a null or unaligned base would
+            // make the copies fault, so refuse it and drain instead
+            if (kb == nullptr || vb == nullptr ||
+                ((reinterpret_cast<uintptr_t>(kb) | reinterpret_cast<uintptr_t>(vb)) & 15u)) {
+              atomicCAS(a.status, 0, GLA_ERR_ALIGNMENT);
+              flags[0] = 1;
+              break;
+            }
+          }
+          const int rows = min(a.tile, npos[tr.b] - row0);
+          constexpr int kCpr = HD * esize / 16;  // 16-byte chunks per row
+          for (int idx = lane; idx < rows * kCpr; idx += 32) {
+            const int r = idx / kCpr, c = idx - r * kCpr;
+            const int64_t off =
+                ((int64_t)(row0 + r) * a.kv_stride + (int64_t)tr.g * HD) * esize + c * 16;
+            const int soff = TL::chunk_off(a.tile, r, c * (16 / esize));
+            cp_async_16(ks + soff, kb + off, pol);
+            cp_async_16(vs + soff, vb + off, pol);
+          }
+          cp_async_arrive_noinc(&full[st]);
         }
         next_tile(tr, ntiles, B, n_kv);
       }
@@ -578,6 +639,88 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodeAr
   float* merge_w = merge + warp * kMG * (HD + 2);
   TileRef tr = locate_tile(seq_start, ntiles, B, n_kv, my_lo);
   int cur_b = -1, cur_g = -1;
+  constexpr int kSH = slot_head_floats<HD>();
+  float* comb = reinterpret_cast<float*>(smem + a.off_comb);  // [2][P][kMaxGroup] + [2][kMaxGroup]
+
+  // The group's q vectors, pre-scaled by scale*log2(e), rows >= G zeroed.
+  auto load_q = [&](int b, int g) {
+    const float* qb = a.q + ((int64_t)b * a.n_heads + (int64_t)g * G) * HD;
+    for (int i = tid; i < kMaxGroup * HD; i += kNCT) qs[i] = i < G * HD ? qb[i] * a.q_scale : 0.f;
+    consumer_sync(kNCT);
+  };
+
+  // Merges the pieces of segment (b, g) held in workspace slots c + s for
+  // c in [c0, c0 + npieces): log-sum-exp weights per (piece, head) first,
+  // then every (head, 4 columns) element with independent float4 loads.
+  auto combine_pieces = [&](int b, int g, int s, int c0, int npieces) {
+    float* mb = comb;                          // [npieces][kMaxGroup] m, then weights
+    float* lb = comb + gridDim.x * kMaxGroup;  // [npieces][kMaxGroup] l
+    float* MLb = lb + gridDim.x * kMaxGroup;   // M[kMaxGroup], L[kMaxGroup]
+    // (m, l) of every (piece, head): loads issued four deep per thread
+    for (int p0 = 0; p0 < npieces * G; p0 += 4 * kNCT) {
+      float mv[4], lv[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int p = p0 + tid + k * kNCT;
+        mv[k] = -INFINITY;
+        lv[k] = 0.f;
+        if (p < npieces * G) {
+          const int c = p / G, h = p - c * G;
+          const float* sl = a.ws_part + ((int64_t)(c0 + c + s) * G + h) * kSH;
+          mv[k] = ld_cg(sl + HD);
+          lv[k] = ld_cg(sl + HD + 1);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int p = p0 + tid + k * kNCT;
+        if (p < npieces * G) {
+          const int c = p / G, h = p - c * G;
+          mb[c * kMaxGroup + h] = mv[k];
+          lb[c * kMaxGroup + h] = lv[k];
+        }
+      }
+    }
+    consumer_sync(kNCT);
+    for (int h = warp; h < G; h += NW) {  // one warp per head, lanes over pieces
+      float M = -INFINITY;
+      for (int c = lane; c < npieces; c += 32) M = fmaxf(M, mb[c * kMaxGroup + h]);
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      float L = 0.f;
+      for (int c = lane; c < npieces; c += 32) {
+        const float w = (M == -INFINITY) ? 0.f : fast_exp2(mb[c * kMaxGroup + h] - M);
+        mb[c * kMaxGroup + h] = w;
+        L += w * lb[c * kMaxGroup + h];
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+      if (lane == 0) {
+        MLb[h] = M;
+        MLb[kMaxGroup + h] = L;
+      }
+    }
+    consumer_sync(kNCT);
+    constexpr int kD4 = HD / 4;
+    const int64_t step = (int64_t)G * kSH;
+    for (int idx = tid; idx < G * kD4; idx += kNCT) {
+      const int h = idx / kD4, d = (idx - h * kD4) * 4;
+      const float* base = a.ws_part + ((int64_t)(c0 + s) * G + h) * kSH + d;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c = 0; c < npieces; c += 16) {  // 16 predicated loads in flight
+        float4 v[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u)
+          v[u] = (c + u < npieces) ? ld_cg4(base + (c + u) * step) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const float w = (c + u < npieces) ? mb[(c + u) * kMaxGroup + h] : 0.f;
+          acc.x += w * v[u].x; acc.y += w * v[u].y; acc.z += w * v[u].z; acc.w += w * v[u].w;
+        }
+      }
+      write_final4<HD>(a, b, g * G + h, d, acc, MLb[h], MLb[kMaxGroup + h]);
+    }
+  };
 
   auto finish_piece = [&](int b, int g) {
     cons.to_merge(a, merge_w, lane);
@@ -585,7 +728,6 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodeAr
     const int s = b * n_kv + g;
     int32_t c0;
     const int32_t npieces = segment_pieces(sp, seq_start, ntiles, b, g, &c0);
-    const int slot_floats = G * (HD + 2);
     for (int idx = tid; idx < G * HD; idx += kNCT) {
       const int h = idx / HD, d = idx - h * HD;
       float M = -INFINITY;
@@ -604,7 +746,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodeAr
       if (npieces == 1) {
         write_final<HD>(a, b, g * G + h, d, O, M, L);
       } else {
-        float* slot = a.ws_part + (int64_t)(blockIdx.x + s) * slot_floats + h * (HD + 2);
+        float* slot = a.ws_part + ((int64_t)(blockIdx.x + s) * G + h) * kSH;
         slot[d] = O;
         if (d == 0) {
           slot[HD] = M;
@@ -613,31 +755,14 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodeAr
       }
     }
     if (npieces > 1) {
-      __threadfence();
       consumer_sync(kNCT);
       if (tid == 0) {
-        const int old = atomicAdd(&a.ws_counter[s], 1);
+        const int old = atomic_add_acq_rel_gpu(&a.ws_counter[s], 1);
         flags[1] = (old == npieces - 1) ? 1 : 0;
       }
       consumer_sync(kNCT);
       if (flags[1]) {
-        __threadfence();
-        for (int idx = tid; idx < G * HD; idx += kNCT) {
-          const int h = idx / HD, d = idx - h * HD;
-          float M = -INFINITY;
-          for (int c = c0; c < c0 + npieces; ++c)
-            M = fmaxf(M, ld_cg(a.ws_part + (int64_t)(c + s) * slot_floats + h * (HD + 2) + HD));
-          float O = 0.f, L = 0.f;
-          if (M != -INFINITY) {
-            for (int c = c0; c < c0 + npieces; ++c) {
-              const float* sl = a.ws_part + (int64_t)(c + s) * slot_floats + h * (HD + 2);
-              const float sc = fast_exp2(ld_cg(sl + HD) - M);
-              O += sc * ld_cg(sl + d);
-              L += sc * ld_cg(sl + HD + 1);
-            }
-          }
-          write_final<HD>(a, b, g * G + h, d, O, M, L);
-        }
+        combine_pieces(b, g, s, c0, npieces);
         if (tid == 0) a.ws_counter[s] = 0;
       }
     }
@@ -649,13 +774,14 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodeAr
       if (cur_b >= 0) finish_piece(cur_b, cur_g);
       cur_b = tr.b;
       cur_g = tr.g;
-      cons.begin(a, cur_b, cur_g, lane);
+      load_q(cur_b, cur_g);
+      cons.begin(a, qs, lane);
     }
     const int st = i % a.stages;
     const uint32_t use = (uint32_t)(i / a.stages);
     const int rows = min(a.tile, npos[tr.b] - tr.j * a.tile);
     mbar_wait(&full[st], use & 1u, flags, a.status);
-    cons.consume(a, smem + (size_t)st * a.stage_bytes, rows, pbuf_w, warp, lane);
+    cons.consume(a, smem + (size_t)st * a.stage_bytes, rows, pbuf_w, qs, warp, lane);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
     next_tile(tr, ntiles, B, n_kv);

@@ -3,11 +3,12 @@
 // split-KV work partition used identically by kernels and host code.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/gpullama_attn.h"
+#include "gpullama_attn.h"
 
 #define GLA_HD __host__ __device__ __forceinline__
 
@@ -192,6 +193,35 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Tiled TMA load of a 2D box at (x, y) of `tmap` (a __grid_constant__ kernel
+// parameter) into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tmap, int32_t x,
+                                            int32_t y, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
+// 16-byte cp.async (L2 only) global -> shared with an L2 cache hint.
+__device__ __forceinline__ void cp_async_16(void* dst, const void* src, uint64_t policy) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)),
+               "l"(src), "l"(policy)
+               : "memory");
+}
+
+// Arrives on `bar` once all earlier cp.async of this thread have landed
+// (the arrival is pre-counted in the barrier's expected count).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -205,6 +235,26 @@ __device__ __forceinline__ void consumer_sync(int nthreads) {
 }
 
 __device__ __forceinline__ float ld_cg(const float* p) { return __ldcg(p); }
+
+__device__ __forceinline__ float4 ld_cg4(const float* p) {
+  return __ldcg(reinterpret_cast<const float4*>(p));
+}
+
+// Release/acquire add at GPU scope (one thread, after a CTA barrier: the
+// release covers every write the CTA made before the barrier).
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int32_t* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
+// Programmatic dependent launch: wait for the preceding grid's memory, and
+// let the next grid start its prologue early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 __device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
 
