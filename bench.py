@@ -379,7 +379,7 @@ def run_ours(args, rank, world, local_rank, dist):
         sampler.start()
     t_soak = time.perf_counter()
     per_iter = max(ms_est(replay, stream, torch, device), 1e-3)
-    soak_iters = int(min(5000, max(1, 1000.0 / per_iter)))
+    soak_iters = 0 if args.quick else int(min(5000, max(1, 1000.0 / per_iter)))
     with torch.cuda.stream(stream):
         for _ in range(soak_iters):
             replay()
@@ -408,7 +408,7 @@ def run_ours(args, rank, world, local_rank, dist):
 
     # ---- e2e through the reference-facing call with host buffers -------------
     e2e = None
-    if args.workload in ("c1", "c2"):
+    if args.workload in ("c1", "c2") and not args.quick:
         e2e = run_e2e(args, ctx, wl, inp, torch, device, stream, dist)
 
     del graph
@@ -457,7 +457,7 @@ def run_ours(args, rank, world, local_rank, dist):
     }
     if e2e is not None:
         result["e2e"] = e2e
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.quick):
         result["cpu_baseline"] = cpu_baseline(args.workload, wl)
     ctx.close()
     return result
@@ -616,6 +616,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--quick", action="store_true",
+                    help="profiling runs: no clock soak, no e2e loop, no CPU baseline")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3  # timing rule: at least 3 warm-up steps
