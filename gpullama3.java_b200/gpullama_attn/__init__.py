@@ -71,6 +71,7 @@ _SIGS = {
     "gla_prefill_causal_f16": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _F]),
     "gla_rope_append_f32": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P, _F, _I32]),
     "gla_debug_partition": (_I64, [_P, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _I64]),
+    "gla_decode_f32kv_noalloc": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F, _P]),
 }
 
 EXPORTED_SYMBOLS = tuple(_SIGS)

@@ -203,6 +203,28 @@ int32_t gla_decode_partial_f16kv(gla_ctx* ctx, const float* q, const uint16_t* k
 int32_t gla_lse_combine(gla_ctx* ctx, const float* parts, int32_t n_parts, int32_t n_heads,
                         int32_t head_dim, float* xb);
 
+/* Allocation-free FP32-cache decode.  No counterpart in the reference: it
+ * serves callers that cannot allocate device memory where they need
+ * attention (buffers owned by another runtime such as TornadoVM, allocators
+ * that forbid growth mid-step, embedders that must not call cudaMalloc/cudaFree
+ * because those synchronise the device) - gla_create allocates, this does not.
+ * Same arguments and result as gla_decode_f32kv, on the CURRENT device and on
+ * `cuda_stream` (a cudaStream_t; NULL = legacy default stream); no context.
+ * Scratch: a fixed 1 MiB + 8 KiB static device array of the library, held by
+ * every GPU that loads it until exit.  The first call on a device looks up
+ * that array's address (cudaGetSymbolAddress): make it before any stream
+ * capture.  Limits: (number of SMs + n_kv_heads) * kvMul * (head_dim + 4)
+ * floats of partial records must fit in 1 MiB and n_kv_heads <= 1024, else
+ * GLA_ERR_NOT_SUPPORTED; head_dim 64/96/128 and kvMul <= 8 as for
+ * gla_decode_f32kv.  Every call shares the array (each call clears the
+ * counters it uses first), so calls whose kernels overlap on the GPU race.
+ * A bounded device wait that gives up is not reported (there is no context
+ * to read it from). */
+int32_t gla_decode_f32kv_noalloc(const float* q, const float* k, const float* v, float* xb,
+                                 int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                 int64_t kv_stride, int32_t n_pos, float scale,
+                                 void* cuda_stream);
+
 /* ------------------------------------------------------------------------ */
 /* Multi-GPU: KV-sequence sharded decode over NCCL                           */
 /* ------------------------------------------------------------------------ */
