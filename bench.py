@@ -269,6 +269,7 @@ def cpu_baseline(wl_key, wl, budget_s=8.0, full_step=False):
 def run_ours(args, rank, world, local_rank, dist):
     import torch
     import gpullama_attn as gla
+    from gpullama_attn import sharding
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
@@ -283,20 +284,12 @@ def run_ours(args, rank, world, local_rank, dist):
     lengths = None
     if args.workload == "c3":
         all_len = c3_lengths()
-        order = sorted(range(len(all_len)), key=lambda i: -all_len[i])
-        loads = [0] * world
-        mine = []
-        for i in order:  # longest-processing-time assignment
-            r = min(range(world), key=lambda j: loads[j])
-            loads[r] += all_len[i]
-            if r == rank:
-                mine.append(all_len[i])
-        lengths = mine
+        lengths = [all_len[i] for i in sharding.lpt_assign(all_len, world)[rank]]
         scaling = "strong"
         rows_step = sum(all_len)
     elif args.workload == "c4":
         T = wl["T"]
-        lo, hi = rank * T // world, (rank + 1) * T // world
+        lo, hi = sharding.kv_shard_bounds(T, world, rank)
         scaling = "strong"
         rows_step = T
     else:
