@@ -1,15 +1,495 @@
-// prefill.cu - causal prefill attention (tcgen05 / TMEM); placeholder until
-// the tensor-core kernel lands.
+// prefill.cu - causal prefill attention on tcgen05 tensor cores with TMEM
+// accumulators (sm_100a).
+//
+// out[p][h] = softmax_{t <= p}(scale * q[p][h] . k[t][g]) . v[t][g], g = h / kvMul,
+// for a whole prompt at once: what the reference computes one position at a
+// time while it ingests a prompt (InferenceEngine.java:88-99, one
+// InferenceCore.forwardJava attention block per position).
+//
+// One CTA per (head, 128-row query block), heaviest blocks first:
+//   warp 4     producer: TMA loads of the Q block once, then K/V blocks of 128
+//              keys into a 2-stage ring (SWIZZLE_64B, 32-half column blocks).
+//   warp 5     MMA issuer (one thread): S_j = Q K_j^T into TMEM (double
+//              buffered, 128 columns each), then O += P_j V_j into a TMEM
+//              accumulator; tcgen05.commit signals mbarriers.
+//   warps 0-3  softmax: thread r owns query row r, reads its 128 scores with
+//              tcgen05.ld, keeps the row max/sum in registers (no shuffles),
+//              writes P_j (FP16) to a swizzled shared-memory buffer for the
+//              second MMA, and rescales O in TMEM only when the row max grows
+//              by more than 2^8 (otherwise p <= 2^8 stays exact in FP16 and
+//              the final division by l absorbs the stale max).
+// FP32 softmax and accumulation; FP16 inputs; FP32 output.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+#include <string>
+
 #include "gla_common.cuh"
 #include "gla_internal.h"
 
 namespace gla {
 
-int launch_prefill_f16(const uint16_t*, const uint16_t*, const uint16_t*, float*, int32_t,
-                       int32_t, int32_t, int32_t, float, int32_t*, const DeviceInfo&,
-                       cudaStream_t, std::string* err) {
-  *err = "prefill kernel not built yet";
-  return GLA_ERR_NOT_SUPPORTED;
+namespace {
+
+constexpr int kBM = 128;       // query rows per CTA
+constexpr int kBN = 128;       // keys per block
+constexpr int kStages = 2;     // K/V ring depth
+constexpr int kThreads = 192;  // 4 softmax warps + producer + MMA
+constexpr float kRescaleLog2 = 8.0f;
+
+struct PrefillArgs {
+  CUtensorMap tq;  // [L][n_heads*hd]    box (32, 128), SWIZZLE_64B
+  CUtensorMap tk;  // [L][n_kv*hd]       box (32, 128)
+  CUtensorMap tv;
+  float* out;      // [L][n_heads*hd] FP32
+  int32_t L;
+  int32_t n_heads;
+  int32_t kv_mul;
+  int32_t n_qblocks;
+  float scale_log2;
+  int32_t* status;
+};
+
+// ---- tcgen05 / TMEM wrappers ----------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 32 lanes x 32 columns of 32-bit: thread i of the warp gets lane (warp%4)*32+i.
+// The wait sits in the same asm statement so no use of the registers can be
+// scheduled before the load has landed.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor, SWIZZLE_64B (layout type 4), version 1.
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr, uint32_t lbo_bytes,
+                                                   uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version (Blackwell)
+  d |= (uint64_t)4 << 61;  // SWIZZLE_64B
+  return d;
+}
+
+// Instruction descriptor for kind::f16: F16 x F16 -> F32, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool b_mn_major) {
+  return (1u << 4)                          // D format F32
+         | (0u << 7) | (0u << 10)           // A, B format F16
+         | (0u << 15)                       // A K-major
+         | ((b_mn_major ? 1u : 0u) << 16)   // B major
+         | ((uint32_t)(N >> 3) << 17)       // N / 8
+         | ((uint32_t)(M >> 4) << 24);      // M / 16
+}
+
+// Byte offset, inside a [blocks][rows][32 halves] SWIZZLE_64B tile, of the
+// 16-byte chunk `c` (0..3) of `row` in column block `cb`.
+__device__ __forceinline__ uint32_t sw64_off(int rows, int cb, int row, int c) {
+  return (uint32_t)(cb * rows * 64 + row * 64 + ((c ^ ((row >> 1) & 3)) << 4));
+}
+
+template <int HD>
+struct PrefillSmem {
+  static constexpr int kCB = HD / 32;                  // 32-half column blocks
+  static constexpr int kQBytes = kBM * HD * 2;
+  static constexpr int kKVBytes = kBN * HD * 2;        // one of K or V
+  static constexpr int kPBytes = kBM * kBN * 2;        // P block, FP16
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kOffQ + kQBytes;
+  static constexpr int kOffV = kOffK + kStages * kKVBytes;
+  static constexpr int kOffP = kOffV + kStages * kKVBytes;
+  static constexpr int kOffBar = kOffP + 2 * kPBytes;
+  // barriers: q_full, kv_full[2], kv_empty[2], s_full[2], s_empty[2], p_full[2], pdone[2],
+  // mma_done
+  static constexpr int kNumBars = 1 + 2 * kStages + 9;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr int kBytes = kOffMisc + 32;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillArgs a) {
+  using SM = PrefillSmem<HD>;
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // heaviest (longest causal range) query blocks first
+  const int qb = a.n_qblocks - 1 - (int)(blockIdx.x / a.n_heads);
+  const int h = (int)(blockIdx.x % a.n_heads);
+  const int g = h / a.kv_mul;
+  const int nb = qb + 1;  // key blocks 0..qb (causal)
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kOffBar);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + kStages;
+  uint64_t* s_full = kv_empty + kStages;
+  uint64_t* s_empty = s_full + 2;
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* pdone = p_full + 2;
+  uint64_t* mma_done = pdone + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SM::kOffMisc + 8);
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_empty[b], 4);
+      mbar_init(&p_full[b], 4);
+      mbar_init(&pdone[b], 1);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 512);  // S0 [0,128) S1 [128,256) O [256, 256+HD)
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS[2] = {tmem, tmem + 128};
+  const uint32_t tO = tmem + 256;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------- producer
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first_policy();
+      char* sq = smem + SM::kOffQ;
+      mbar_arrive_expect_tx(q_full, SM::kQBytes);
+#pragma unroll
+      for (int cb = 0; cb < SM::kCB; ++cb)
+        tma_load_2d(sq + cb * kBM * 64, &a.tq, h * HD + cb * 32, qb * kBM, q_full, pol);
+      for (int j = 0; j < nb; ++j) {
+        const int st = j % kStages;
+        const uint32_t use = (uint32_t)(j / kStages);
+        if (!mbar_wait(&kv_empty[st], (use & 1u) ^ 1u, abort_flag, a.status)) break;
+        char* sk = smem + SM::kOffK + st * SM::kKVBytes;
+        char* sv = smem + SM::kOffV + st * SM::kKVBytes;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * SM::kKVBytes);
+#pragma unroll
+        for (int cb = 0; cb < SM::kCB; ++cb) {
+          tma_load_2d(sk + cb * kBN * 64, &a.tk, g * HD + cb * 32, j * kBN, &kv_full[st], pol);
+          tma_load_2d(sv + cb * kBN * 64, &a.tv, g * HD + cb * 32, j * kBN, &kv_full[st], pol);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdS = idesc_f16(kBM, kBN, false);
+      constexpr uint32_t kIdO = idesc_f16(kBM, HD, true);
+      const uint32_t sq = smem_u32(smem + SM::kOffQ);
+      bool ok = mbar_wait(q_full, 0, abort_flag, a.status);
+      auto issue_pv = [&](int jj) {
+        const int b = jj & 1, st = jj % kStages;
+        ok = ok && mbar_wait(&p_full[b], (uint32_t)((jj >> 1) & 1), abort_flag, a.status);
+        tc_fence_after();
+        const uint32_t sp = smem_u32(smem + SM::kOffP + b * SM::kPBytes);
+        const uint32_t sv = smem_u32(smem + SM::kOffV + st * SM::kKVBytes);
+#pragma unroll
+        for (int k = 0; k < kBN / 16; ++k) {
+          // A = P (K-major over keys): column block k/2, 32-byte half k%2
+          const uint64_t ad = smem_desc_sw64(sp + (k >> 1) * kBM * 64 + (k & 1) * 32, 16, 512);
+          // B = V (MN-major: hd contiguous): 16 keys = two 8-row atoms of 512 B;
+          // LBO = stride between 32-half column blocks of hd
+          const uint64_t bd = smem_desc_sw64(sv + k * 1024, kBN * 64, 512);
+          tc_mma_f16(tO, ad, bd, kIdO, (jj > 0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(&pdone[b]);
+        tc_commit(&kv_empty[st]);
+      };
+      for (int j = 0; j < nb; ++j) {
+        const int st = j % kStages, b = j & 1;
+        ok = ok && mbar_wait(&kv_full[st], (uint32_t)((j / kStages) & 1), abort_flag, a.status);
+        if (j >= 2) ok = ok && mbar_wait(&s_empty[b], (uint32_t)(((j - 2) >> 1) & 1), abort_flag, a.status);
+        tc_fence_after();
+        const uint32_t sk = smem_u32(smem + SM::kOffK + st * SM::kKVBytes);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          const uint32_t off = (k >> 1) * kBM * 64 + (k & 1) * 32;
+          const uint64_t ad = smem_desc_sw64(sq + off, 16, 512);
+          const uint64_t bd = smem_desc_sw64(sk + (k >> 1) * kBN * 64 + (k & 1) * 32, 16, 512);
+          tc_mma_f16(tS[b], ad, bd, kIdS, k > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[b]);
+        if (j >= 1) issue_pv(j - 1);
+      }
+      issue_pv(nb - 1);
+      // every MMA of this CTA has finished before TMEM is released (also on
+      // the drain path after a timed-out wait)
+      tc_commit(mma_done);
+      volatile int no_abort = 0;
+      mbar_wait(mma_done, 0, &no_abort, a.status);
+    }
+  } else {
+    // ------------------------------------------------------------- softmax
+    const int r = tid;                 // query row inside the block (== TMEM lane)
+    const int qi = qb * kBM + r;       // query position
+    const uint32_t lane_sel = (uint32_t)(warp * 32) << 16;
+    float m_ref = -INFINITY, l = 0.f;
+    for (int j = 0; j < nb; ++j) {
+      const int b = j & 1;
+      mbar_wait(&s_full[b], (uint32_t)((j >> 1) & 1), abort_flag, a.status);
+      tc_fence_after();
+      float s[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        float t[32];
+        tmem_ld32(tS[b] + lane_sel + c * 32, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = t[i];
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[b]);
+      float mx = -INFINITY;
+      const bool diag = (j == qb);
+#pragma unroll
+      for (int c = 0; c < kBN; ++c) {
+        float x = s[c] * a.scale_log2;
+        if (diag && (j * kBN + c > qi)) x = -INFINITY;
+        s[c] = x;
+        mx = fmaxf(mx, x);
+      }
+      if (j == 0) {
+        m_ref = mx;
+      } else if (__any_sync(0xffffffffu, mx > m_ref + kRescaleLog2)) {
+        // O holds sum_t 2^(s_t - m_ref) v_t: wait for the last P.V, rescale it
+        mbar_wait(&pdone[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1), abort_flag, a.status);
+        tc_fence_after();
+        const float mnew = fmaxf(m_ref, mx);
+        const float alpha = fast_exp2(m_ref - mnew);
+        l *= alpha;
+        m_ref = mnew;
+#pragma unroll
+        for (int c = 0; c < (HD + 31) / 32; ++c) {
+          float t[32];
+          tmem_ld32(tO + lane_sel + c * 32, t);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) t[i] *= alpha;
+          tmem_st32(tO + lane_sel + c * 32, t);
+        }
+        tmem_wait_st();
+      }
+      // p = 2^(s - m_ref) <= 2^8, FP16 into the swizzled P buffer b
+      if (j >= 2) mbar_wait(&pdone[b], (uint32_t)(((j - 2) >> 1) & 1), abort_flag, a.status);
+      char* pb = smem + SM::kOffP + b * SM::kPBytes;
+      float rs = 0.f;
+#pragma unroll
+      for (int ch = 0; ch < kBN / 8; ++ch) {  // 16-byte chunks of 8 keys
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = fast_exp2(s[ch * 8 + 2 * e] - m_ref);
+          const float p1 = fast_exp2(s[ch * 8 + 2 * e + 1] - m_ref);
+          rs += p0 + p1;
+          const __half2 hp = __floats2half2_rn(p0, p1);
+          w[e] = *reinterpret_cast<const uint32_t*>(&hp);
+        }
+        const uint32_t off = sw64_off(kBM, ch >> 2, r, ch & 3);
+        *reinterpret_cast<uint4*>(pb + off) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l += rs;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
+    }
+    // epilogue: O / l
+    mbar_wait(&pdone[(nb - 1) & 1], (uint32_t)(((nb - 1) >> 1) & 1), abort_flag, a.status);
+    tc_fence_after();
+    const float inv = 1.f / l;
+    float* orow = a.out + (int64_t)qi * a.n_heads * HD + (int64_t)h * HD;
+    const bool store = qi < a.L;
+#pragma unroll
+    for (int c = 0; c < HD / 32; ++c) {
+      float t[32];
+      tmem_ld32(tO + lane_sel + c * 32, t);
+      tmem_wait_ld();
+      if (store) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(orow + c * 32 + i) =
+              make_float4(t[i] * inv, t[i + 1] * inv, t[i + 2] * inv, t[i + 3] * inv);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn_prefill() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool encode_f16_rows(CUtensorMap* map, const void* base, int64_t width, int64_t rows,
+                     std::string* err) {
+  auto fn = encode_fn_prefill();
+  if (!fn) {
+    *err = "cuTensorMapEncodeTiled unavailable";
+    return false;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)width, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(width * 2)};
+  cuuint32_t box[2] = {32, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *err = "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")";
+    return false;
+  }
+  return true;
+}
+
+template <int HD>
+int launch_hd(const PrefillArgs& a, int grid, cudaStream_t stream, std::string* err) {
+  const size_t smem = PrefillSmem<HD>::kBytes + 1024;
+  cudaFuncSetAttribute(prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)smem);
+  prefill_kernel<HD><<<grid, kThreads, smem, stream>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    *err = std::string("prefill launch failed: ") + cudaGetErrorString(e);
+    return GLA_ERR_CUDA;
+  }
+  return GLA_OK;
+}
+
+}  // namespace
+
+int launch_prefill_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v, float* out,
+                       int32_t L, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                       float scale, int32_t* status, const DeviceInfo& dev, cudaStream_t stream,
+                       std::string* err) {
+  if (!(head_dim == 64 || head_dim == 96 || head_dim == 128)) {
+    *err = "prefill head_dim must be 64, 96 or 128";
+    return GLA_ERR_NOT_SUPPORTED;
+  }
+  const size_t need = (head_dim == 64    ? PrefillSmem<64>::kBytes
+                       : head_dim == 96 ? PrefillSmem<96>::kBytes
+                                        : PrefillSmem<128>::kBytes) +
+                      1024;
+  if (need > (size_t)dev.smem_optin) {
+    *err = "prefill shared memory layout does not fit";
+    return GLA_ERR_NOT_SUPPORTED;
+  }
+  if (((int64_t)n_heads * head_dim * 2) % 16 != 0 || ((int64_t)n_kv_heads * head_dim * 2) % 16)
+    {
+    *err = "prefill row widths must be multiples of 16 bytes";
+    return GLA_ERR_ALIGNMENT;
+  }
+  PrefillArgs a{};
+  if (!encode_f16_rows(&a.tq, q, (int64_t)n_heads * head_dim, L, err) ||
+      !encode_f16_rows(&a.tk, k, (int64_t)n_kv_heads * head_dim, L, err) ||
+      !encode_f16_rows(&a.tv, v, (int64_t)n_kv_heads * head_dim, L, err))
+    return GLA_ERR_INVALID_ARG;
+  a.out = out;
+  a.L = L;
+  a.n_heads = n_heads;
+  a.kv_mul = n_heads / n_kv_heads;
+  a.n_qblocks = (L + kBM - 1) / kBM;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.status = status;
+  const int grid = a.n_qblocks * n_heads;
+  switch (head_dim) {
+    case 64: return launch_hd<64>(a, grid, stream, err);
+    case 96: return launch_hd<96>(a, grid, stream, err);
+    default: return launch_hd<128>(a, grid, stream, err);
+  }
 }
 
 }  // namespace gla
