@@ -52,6 +52,8 @@ WORKLOADS = {
                T=None, f16=True, theta=None, batch=16),
     "c4": dict(name="qwen2.5-7b-longctx-decode-attn", layers=1, n_heads=28, n_kv=4, hd=128,
                T=131072, f16=True, theta=None, batch=1),
+    "c5": dict(name="phi3-mini-causal-prefill-attn", layers=1, n_heads=32, n_kv=32, hd=96,
+               T=4096, f16=True, theta=None, batch=1),
 }
 
 FALLBACK_HBM_GBS = 6650.0
@@ -494,6 +496,129 @@ def ms_est(fn, stream, torch, device):
     return e0.elapsed_time(e1)
 
 
+def run_prefill(args, rank, world, local_rank, dist):
+    """causal prefill, L 4096, 32 heads, hd 96, FP16 in, FP32
+    softmax/accumulation/out. Metric: causal TFLOP/s = 4*nH*hd*L(L+1)/2 / time."""
+    import torch
+    import gpullama_attn as gla
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    wl = WORKLOADS["c5"]
+    L, nh, nkv, hd = wl["T"], wl["n_heads"], wl["n_kv"], wl["hd"]
+    stream = torch.cuda.Stream(device)
+    ctx = gla.Context(local_rank, stream.cuda_stream)
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    with torch.cuda.stream(stream):
+        q = torch.randn(L, nh * hd, device=device, generator=g).half()
+        k = torch.randn(L, nkv * hd, device=device, generator=g).half()
+        v = torch.randn(L, nkv * hd, device=device, generator=g).half()
+        out = torch.empty(L, nh * hd, device=device)
+        # rotate inputs through copies larger than L2 so successive launches
+        # read from HBM (Q/K/V are 25 MB each)
+        n_rot = 3
+        qs = [q.clone() for _ in range(n_rot)]
+        ks = [k.clone() for _ in range(n_rot)]
+        vs = [v.clone() for _ in range(n_rot)]
+    torch.cuda.synchronize(device)
+
+    def step(i):
+        r = i % n_rot
+        ctx.prefill_causal(qs[r], ks[r], vs[r], out, L, nh, nkv, hd)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+    torch.cuda.synchronize(device)
+    if ctx.device_status() != 0:
+        raise RuntimeError("device status after warm-up")
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    t_soak = time.perf_counter()
+    if not args.quick:
+        per = max(ms_est(lambda: step(0), stream, torch, device), 1e-3)
+        with torch.cuda.stream(stream):
+            for i in range(int(min(20000, 1000.0 / per))):
+                step(i)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    soak_s = time.perf_counter() - t_soak
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / args.steps
+    clocks = sampler.stop() if sampler else None
+    if dist is not None:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if ctx.device_status() != 0:
+        raise RuntimeError("device status after the timed region")
+    flops = 4.0 * nh * hd * L * (L + 1) / 2
+    tflops = flops / (ms * 1e-3) / 1e12 * world
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        peak, peak_kind = float(pk["bf16_tflops"]), "measured cuBLAS bf16 burst (MEASURED_PEAKS.json)"
+    except Exception:
+        peak, peak_kind = 1590.0, "fallback 1.59 PFLOP/s"
+    # e2e: pinned host Q/K/V in, output back, through the C ABI
+    hq = q.cpu().pin_memory()
+    hk = k.cpu().pin_memory()
+    hv = v.cpu().pin_memory()
+    hout = torch.empty(L, nh * hd).pin_memory()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        ctx.prefill_causal(dq, dk, dv, out, L, nh, nkv, hd)
+        hout.copy_(out, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize(device)
+        w0 = time.perf_counter()
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = max(e0.elapsed_time(e1), (time.perf_counter() - w0) * 1e3) / args.steps
+    res = {
+        "metric": "prefill-attn TFLOP/s (causal)", "value": round(tflops, 2), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16-in f32-softmax/acc f32-out",
+        "data": "synthetic ~N(0,1), seeded torch generator",
+        "config": {"workload": wl["name"], "baseline_config": "c5", "L": L, "n_heads": nh,
+                   "n_kv_heads": nkv, "head_dim": hd, "causal": True,
+                   "l2": "3 rotating Q/K/V copies (75 MB each set, 226 MB total > 126 MB L2)",
+                   "parallelism": f"replicas{world}" if world > 1 else "single"},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "tensor", "achieved": round(tflops / world, 2), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(tflops / world / peak, 4), "traffic": None,
+                     "peak_source": peak_kind, "kernel": "gla::prefill_kernel<96>",
+                     "flops_per_launch": flops},
+        "clocks": dict(clocks, soak_s=round(soak_s, 2)) if clocks else None,
+        "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12 * world, 2), "unit": "TFLOP/s",
+                "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": int((q.numel() + k.numel() + v.numel()) * 2),
+                "d2h_bytes_per_step": int(out.numel() * 4)},
+    }
+    ctx.close()
+    return res
+
+
 def run_e2e(args, ctx, wl, inp, torch, device, stream, dist):
     """Per step: one H2D of the token's q (all layers) and new k/v rows from pinned
     memory, then per layer RoPE + KV append + attention through the
@@ -663,7 +788,10 @@ def main():
                                  device_id=torch.device("cuda", local_rank))
         dist = tdist
     try:
-        res = run_ours(args, rank, world, local_rank, dist)
+        if args.workload == "c5":
+            res = run_prefill(args, rank, world, local_rank, dist)
+        else:
+            res = run_ours(args, rank, world, local_rank, dist)
         if rank == 0:
             print(json.dumps(res), flush=True)
     finally:

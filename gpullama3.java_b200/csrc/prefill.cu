@@ -7,8 +7,10 @@
 // InferenceCore.forwardJava attention block per position).
 //
 // One CTA per (head, 128-row query block), heaviest blocks first:
-//   warp 4     producer: TMA loads of the Q block once, then K/V blocks of 128
-//              keys into a 2-stage ring (SWIZZLE_64B, 32-half column blocks).
+//   warp 4     producer: TMA loads of the Q block once, then K and V blocks of
+//              128 keys into two separate rings (SWIZZLE_64B, 32-half column
+//              blocks): K_j is released as soon as S_j is computed, V_j after
+//              P_j V_j, so the next K tiles stream in while softmax runs.
 //   warp 5     MMA issuer (one thread): S_j = Q K_j^T into TMEM (double
 //              buffered, 128 columns each), then O += P_j V_j into a TMEM
 //              accumulator; tcgen05.commit signals mbarriers.
@@ -35,8 +37,6 @@ namespace {
 
 constexpr int kBM = 128;       // query rows per CTA
 constexpr int kBN = 128;       // keys per block
-constexpr int kStages = 2;     // K/V ring depth
-constexpr int kThreads = 192;  // 4 softmax warps + producer + MMA
 constexpr float kRescaleLog2 = 8.0f;
 
 struct PrefillArgs {
@@ -105,6 +105,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// A whole 128-column row (thread = lane) in one load + wait.
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, float (&v)[128]) {
+  uint32_t r[128];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%128];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]), "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]), "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]), "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]), "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]), "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]), "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]), "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]), "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 128; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 2^x on the MUFU unit (flush-to-zero: subnormal probabilities become 0).
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
@@ -157,27 +175,37 @@ __device__ __forceinline__ uint32_t sw64_off(int rows, int cb, int row, int c) {
   return (uint32_t)(cb * rows * 64 + row * 64 + ((c ^ ((row >> 1) & 3)) << 4));
 }
 
-template <int HD>
+template <int HD, int NT>
 struct PrefillSmem {
   static constexpr int kCB = HD / 32;                  // 32-half column blocks
-  static constexpr int kQBytes = kBM * HD * 2;
-  static constexpr int kKVBytes = kBN * HD * 2;        // one of K or V
+  static constexpr int kQBytes = kBM * HD * 2;         // one Q tile
+  static constexpr int kKVBytes = kBN * HD * 2;        // one K or V block
   static constexpr int kPBytes = kBM * kBN * 2;        // P block, FP16
+  static constexpr int kKS = 2;                        // K ring depth
+  static constexpr int kVS = 2;                        // V ring depth
   static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kOffQ + kQBytes;
-  static constexpr int kOffV = kOffK + kStages * kKVBytes;
-  static constexpr int kOffP = kOffV + kStages * kKVBytes;
-  static constexpr int kOffBar = kOffP + 2 * kPBytes;
-  // barriers: q_full, kv_full[2], kv_empty[2], s_full[2], s_empty[2], p_full[2], pdone[2],
-  // mma_done
-  static constexpr int kNumBars = 1 + 2 * kStages + 9;
+  static constexpr int kOffK = kOffQ + NT * kQBytes;
+  static constexpr int kOffV = kOffK + kKS * kKVBytes;
+  static constexpr int kOffP = kOffV + kVS * kKVBytes;
+  static constexpr int kOffBar = kOffP + NT * kPBytes;
+  // barriers: q_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
+  // per tile s_full, s_empty, p_full, pdone; mma_done
+  static constexpr int kNumBars = 1 + 2 * kKS + 2 * kVS + 4 * NT + 1;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 32;
+  static constexpr int kThreads = (4 * NT + 2) * 32;
 };
 
-template <int HD>
-__global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillArgs a) {
-  using SM = PrefillSmem<HD>;
+// NT query tiles of 128 rows per CTA share every K/V block; tile t has its own
+// softmax warpgroup (warps 4t..4t+3), its own S (128 TMEM columns) and O
+// accumulator (next 128 columns).  The MMA thread alternates between tiles:
+// P_t(j) V_j, then S_t(j+1) = Q_t K_{j+1}^T, so one tile's MMAs run while the
+// other tile's softmax works.
+template <int HD, int NT>
+__global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
+    __maxnreg__(NT == 2 ? 200 : 232) prefill_kernel(const __grid_constant__ PrefillArgs a) {
+  using SM = PrefillSmem<HD, NT>;
+  constexpr int KS = SM::kKS, VS = SM::kVS;
   extern __shared__ __align__(1024) char smem_raw[];
   char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -185,83 +213,107 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   const int qb = a.n_qblocks - 1 - (int)(blockIdx.x / a.n_heads);
   const int h = (int)(blockIdx.x % a.n_heads);
   const int g = h / a.kv_mul;
-  const int nb = qb + 1;  // key blocks 0..qb (causal)
+  const int nb_last = (qb * NT + NT - 1) + 1;  // key blocks of the last tile
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kOffBar);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + kStages;
-  uint64_t* s_full = kv_empty + kStages;
-  uint64_t* s_empty = s_full + 2;
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* pdone = p_full + 2;
-  uint64_t* mma_done = pdone + 2;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + KS;
+  uint64_t* v_full = k_empty + KS;
+  uint64_t* v_empty = v_full + VS;
+  uint64_t* s_full = v_empty + VS;
+  uint64_t* s_empty = s_full + NT;
+  uint64_t* p_full = s_empty + NT;
+  uint64_t* pdone = p_full + NT;
+  uint64_t* mma_done = pdone + NT;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SM::kOffMisc + 8);
 
   if (tid == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int s = 0; s < KS; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], 4);
-      mbar_init(&p_full[b], 4);
-      mbar_init(&pdone[b], 1);
+    for (int s = 0; s < VS; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int t = 0; t < NT; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&s_empty[t], 4);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&pdone[t], 1);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
-  if (warp == 5) {
-    tmem_alloc(tmem_slot, 512);  // S0 [0,128) S1 [128,256) O [256, 256+HD)
+  if (warp == 4 * NT + 1) {
+    tmem_alloc(tmem_slot, 256 * NT);  // tile t: S [256t, 256t+128), O [256t+128, +HD)
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS[2] = {tmem, tmem + 128};
-  const uint32_t tO = tmem + 256;
 
-  if (warp == 4) {
+  if (warp == 4 * NT) {
     // ------------------------------------------------------------- producer
     if (lane == 0) {
       const uint64_t pol = l2_evict_first_policy();
-      char* sq = smem + SM::kOffQ;
-      mbar_arrive_expect_tx(q_full, SM::kQBytes);
+      mbar_arrive_expect_tx(q_full, NT * SM::kQBytes);
 #pragma unroll
-      for (int cb = 0; cb < SM::kCB; ++cb)
-        tma_load_2d(sq + cb * kBM * 64, &a.tq, h * HD + cb * 32, qb * kBM, q_full, pol);
-      for (int j = 0; j < nb; ++j) {
-        const int st = j % kStages;
-        const uint32_t use = (uint32_t)(j / kStages);
-        if (!mbar_wait(&kv_empty[st], (use & 1u) ^ 1u, abort_flag, a.status)) break;
-        char* sk = smem + SM::kOffK + st * SM::kKVBytes;
-        char* sv = smem + SM::kOffV + st * SM::kKVBytes;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * SM::kKVBytes);
+      for (int t = 0; t < NT; ++t)
 #pragma unroll
-        for (int cb = 0; cb < SM::kCB; ++cb) {
-          tma_load_2d(sk + cb * kBN * 64, &a.tk, g * HD + cb * 32, j * kBN, &kv_full[st], pol);
-          tma_load_2d(sv + cb * kBN * 64, &a.tv, g * HD + cb * 32, j * kBN, &kv_full[st], pol);
+        for (int cb = 0; cb < SM::kCB; ++cb)
+          tma_load_2d(smem + SM::kOffQ + t * SM::kQBytes + cb * kBM * 64, &a.tq,
+                      h * HD + cb * 32, (qb * NT + t) * kBM, q_full, pol);
+      // K runs ahead of V: K_j is needed (and freed) one softmax step earlier
+      int jk = 0, jv = 0;
+      while (jk < nb_last || jv < nb_last) {
+        if (jk < nb_last && (jk <= jv + KS - 1 || jv >= nb_last)) {
+          const int st = jk % KS;
+          if (!mbar_wait(&k_empty[st], (uint32_t)(((jk / KS) & 1) ^ 1), abort_flag, a.status)) break;
+          char* sk = smem + SM::kOffK + st * SM::kKVBytes;
+          mbar_arrive_expect_tx(&k_full[st], SM::kKVBytes);
+#pragma unroll
+          for (int cb = 0; cb < SM::kCB; ++cb)
+            tma_load_2d(sk + cb * kBN * 64, &a.tk, g * HD + cb * 32, jk * kBN, &k_full[st], pol);
+          ++jk;
+        } else {
+          const int st = jv % VS;
+          if (!mbar_wait(&v_empty[st], (uint32_t)(((jv / VS) & 1) ^ 1), abort_flag, a.status)) break;
+          char* sv = smem + SM::kOffV + st * SM::kKVBytes;
+          mbar_arrive_expect_tx(&v_full[st], SM::kKVBytes);
+#pragma unroll
+          for (int cb = 0; cb < SM::kCB; ++cb)
+            tma_load_2d(sv + cb * kBN * 64, &a.tv, g * HD + cb * 32, jv * kBN, &v_full[st], pol);
+          ++jv;
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 4 * NT + 1) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t kIdS = idesc_f16(kBM, kBN, false);
       constexpr uint32_t kIdO = idesc_f16(kBM, HD, true);
-      const uint32_t sq = smem_u32(smem + SM::kOffQ);
       bool ok = mbar_wait(q_full, 0, abort_flag, a.status);
-      auto issue_pv = [&](int jj) {
-        const int b = jj & 1, st = jj % kStages;
-        ok = ok && mbar_wait(&p_full[b], (uint32_t)((jj >> 1) & 1), abort_flag, a.status);
-        tc_fence_after();
-        const uint32_t sp = smem_u32(smem + SM::kOffP + b * SM::kPBytes);
-        const uint32_t sv = smem_u32(smem + SM::kOffV + st * SM::kKVBytes);
+      auto issue_s = [&](int t, int j) {  // S_t(j) = Q_t K_j^T
+        const uint32_t sq = smem_u32(smem + SM::kOffQ + t * SM::kQBytes);
+        const uint32_t sk = smem_u32(smem + SM::kOffK + (j % KS) * SM::kKVBytes);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          const uint32_t off = (k >> 1) * kBM * 64 + (k & 1) * 32;
+          const uint64_t ad = smem_desc_sw64(sq + off, 16, 512);
+          const uint64_t bd = smem_desc_sw64(sk + (k >> 1) * kBN * 64 + (k & 1) * 32, 16, 512);
+          tc_mma_f16(tmem + 256 * t, ad, bd, kIdS, k > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) {  // O_t += P_t(j) V_j
+        const uint32_t sp = smem_u32(smem + SM::kOffP + t * SM::kPBytes);
+        const uint32_t sv = smem_u32(smem + SM::kOffV + (j % VS) * SM::kKVBytes);
 #pragma unroll
         for (int k = 0; k < kBN / 16; ++k) {
           // A = P (K-major over keys): column block k/2, 32-byte half k%2
@@ -269,134 +321,149 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
           // B = V (MN-major: hd contiguous): 16 keys = two 8-row atoms of 512 B;
           // LBO = stride between 32-half column blocks of hd
           const uint64_t bd = smem_desc_sw64(sv + k * 1024, kBN * 64, 512);
-          tc_mma_f16(tO, ad, bd, kIdO, (jj > 0 || k > 0) ? 1u : 0u);
+          tc_mma_f16(tmem + 256 * t + 128, ad, bd, kIdO, (j > 0 || k > 0) ? 1u : 0u);
         }
-        tc_commit(&pdone[b]);
-        tc_commit(&kv_empty[st]);
+        tc_commit(&pdone[t]);
       };
-      for (int j = 0; j < nb; ++j) {
-        const int st = j % kStages, b = j & 1;
-        ok = ok && mbar_wait(&kv_full[st], (uint32_t)((j / kStages) & 1), abort_flag, a.status);
-        if (j >= 2) ok = ok && mbar_wait(&s_empty[b], (uint32_t)(((j - 2) >> 1) & 1), abort_flag, a.status);
-        tc_fence_after();
-        const uint32_t sk = smem_u32(smem + SM::kOffK + st * SM::kKVBytes);
-#pragma unroll
-        for (int k = 0; k < HD / 16; ++k) {
-          const uint32_t off = (k >> 1) * kBM * 64 + (k & 1) * 32;
-          const uint64_t ad = smem_desc_sw64(sq + off, 16, 512);
-          const uint64_t bd = smem_desc_sw64(sk + (k >> 1) * kBN * 64 + (k & 1) * 32, 16, 512);
-          tc_mma_f16(tS[b], ad, bd, kIdS, k > 0 ? 1u : 0u);
+      ok = ok && mbar_wait(&k_full[0], 0, abort_flag, a.status);
+      tc_fence_after();
+      for (int t = 0; t < NT; ++t) issue_s(t, 0);
+      tc_commit(&k_empty[0]);
+      for (int j = 0; j < nb_last; ++j) {
+        ok = ok && mbar_wait(&v_full[j % VS], (uint32_t)((j / VS) & 1), abort_flag, a.status);
+        const bool next_k = j + 1 < nb_last;
+        if (next_k)
+          ok = ok && mbar_wait(&k_full[(j + 1) % KS], (uint32_t)(((j + 1) / KS) & 1), abort_flag,
+                               a.status);
+        for (int t = 0; t < NT; ++t) {
+          const int nb_t = qb * NT + t + 1;
+          if (j >= nb_t) continue;
+          ok = ok && mbar_wait(&p_full[t], (uint32_t)(j & 1), abort_flag, a.status);
+          tc_fence_after();
+          issue_pv(t, j);
+          if (j + 1 < nb_t) {
+            ok = ok && mbar_wait(&s_empty[t], (uint32_t)(j & 1), abort_flag, a.status);
+            tc_fence_after();
+            issue_s(t, j + 1);
+          }
         }
-        tc_commit(&s_full[b]);
-        if (j >= 1) issue_pv(j - 1);
+        tc_commit(&v_empty[j % VS]);
+        if (next_k) tc_commit(&k_empty[(j + 1) % KS]);
       }
-      issue_pv(nb - 1);
       // every MMA of this CTA has finished before TMEM is released (also on
       // the drain path after a timed-out wait)
       tc_commit(mma_done);
       volatile int no_abort = 0;
       mbar_wait(mma_done, 0, &no_abort, a.status);
+      (void)ok;
     }
   } else {
     // ------------------------------------------------------------- softmax
-    const int r = tid;                 // query row inside the block (== TMEM lane)
-    const int qi = qb * kBM + r;       // query position
-    const uint32_t lane_sel = (uint32_t)(warp * 32) << 16;
+    const int t = warp >> 2;                  // query tile of this warpgroup
+    const int r = tid & 127;                  // row inside the tile (== TMEM lane)
+    const int qt = qb * NT + t;               // global 128-row block of the tile
+    const int qi = qt * kBM + r;              // query position
+    const int nb = qt + 1;                    // causal key blocks of this tile
+    const uint32_t lane_sel = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + 256 * t + lane_sel;
+    const uint32_t tO = tS + 128;
+    const int wg_bar = 2 + t;                 // named barrier of this warpgroup
+    (void)wg_bar;
     float m_ref = -INFINITY, l = 0.f;
+    const float sl2 = a.scale_log2;
+    char* pb = smem + SM::kOffP + t * SM::kPBytes;
     for (int j = 0; j < nb; ++j) {
-      const int b = j & 1;
-      mbar_wait(&s_full[b], (uint32_t)((j >> 1) & 1), abort_flag, a.status);
+      mbar_wait(&s_full[t], (uint32_t)(j & 1), abort_flag, a.status);
       tc_fence_after();
       float s[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        float t[32];
-        tmem_ld32(tS[b] + lane_sel + c * 32, t);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = t[i];
-      }
-      tmem_wait_ld();
+      tmem_ld128(tS, s);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[b]);
-      float mx = -INFINITY;
-      const bool diag = (j == qb);
+      if (lane == 0) mbar_arrive(&s_empty[t]);
+      // row max of the raw scores (4 independent chains); the causal mask
+      // only touches the diagonal block
+      if (j == qt) {
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) {
-        float x = s[c] * a.scale_log2;
-        if (diag && (j * kBN + c > qi)) x = -INFINITY;
-        s[c] = x;
-        mx = fmaxf(mx, x);
+        for (int c = 0; c < kBN; ++c)
+          if (j * kBN + c > qi) s[c] = -INFINITY;
+      }
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < kBN; c += 4) {
+        m4[0] = fmaxf(m4[0], s[c]);
+        m4[1] = fmaxf(m4[1], s[c + 1]);
+        m4[2] = fmaxf(m4[2], s[c + 2]);
+        m4[3] = fmaxf(m4[3], s[c + 3]);
+      }
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;
+      // P_t(j-1) and O_t: wait until P_t(j-1) V_{j-1} has finished
+      if (j > 0) {
+        mbar_wait(&pdone[t], (uint32_t)((j - 1) & 1), abort_flag, a.status);
+        tc_fence_after();
       }
       if (j == 0) {
         m_ref = mx;
       } else if (__any_sync(0xffffffffu, mx > m_ref + kRescaleLog2)) {
-        // O holds sum_t 2^(s_t - m_ref) v_t: wait for the last P.V, rescale it
-        mbar_wait(&pdone[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1), abort_flag, a.status);
-        tc_fence_after();
+        // O holds sum_t 2^(s_t - m_ref) v_t: rescale it to the new max
         const float mnew = fmaxf(m_ref, mx);
-        const float alpha = fast_exp2(m_ref - mnew);
+        const float alpha = ex2_ftz(m_ref - mnew);
         l *= alpha;
         m_ref = mnew;
 #pragma unroll
         for (int c = 0; c < (HD + 31) / 32; ++c) {
-          float t[32];
-          tmem_ld32(tO + lane_sel + c * 32, t);
-          tmem_wait_ld();
+          float tt[32];
+          tmem_ld32(tO + c * 32, tt);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) t[i] *= alpha;
-          tmem_st32(tO + lane_sel + c * 32, t);
+          for (int i = 0; i < 32; ++i) tt[i] *= alpha;
+          tmem_st32(tO + c * 32, tt);
         }
         tmem_wait_st();
       }
-      // p = 2^(s - m_ref) <= 2^8, FP16 into the swizzled P buffer b
-      if (j >= 2) mbar_wait(&pdone[b], (uint32_t)(((j - 2) >> 1) & 1), abort_flag, a.status);
-      char* pb = smem + SM::kOffP + b * SM::kPBytes;
-      float rs = 0.f;
+      // p = 2^(s - m_ref) <= 2^8, FP16 into the swizzled P buffer of the tile
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int ch = 0; ch < kBN / 8; ++ch) {  // 16-byte chunks of 8 keys
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = fast_exp2(s[ch * 8 + 2 * e] - m_ref);
-          const float p1 = fast_exp2(s[ch * 8 + 2 * e + 1] - m_ref);
-          rs += p0 + p1;
+          const float p0 = ex2_ftz(fmaf(s[ch * 8 + 2 * e], sl2, -m_ref));
+          const float p1 = ex2_ftz(fmaf(s[ch * 8 + 2 * e + 1], sl2, -m_ref));
+          rs4[e] += p0 + p1;
           const __half2 hp = __floats2half2_rn(p0, p1);
           w[e] = *reinterpret_cast<const uint32_t*>(&hp);
         }
         const uint32_t off = sw64_off(kBM, ch >> 2, r, ch & 3);
         *reinterpret_cast<uint4*>(pb + off) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      l += rs;
+      l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[b]);
+      if (lane == 0) mbar_arrive(&p_full[t]);
     }
     // epilogue: O / l
-    mbar_wait(&pdone[(nb - 1) & 1], (uint32_t)(((nb - 1) >> 1) & 1), abort_flag, a.status);
+    mbar_wait(&pdone[t], (uint32_t)((nb - 1) & 1), abort_flag, a.status);
     tc_fence_after();
     const float inv = 1.f / l;
     float* orow = a.out + (int64_t)qi * a.n_heads * HD + (int64_t)h * HD;
     const bool store = qi < a.L;
 #pragma unroll
     for (int c = 0; c < HD / 32; ++c) {
-      float t[32];
-      tmem_ld32(tO + lane_sel + c * 32, t);
-      tmem_wait_ld();
+      float tt[32];
+      tmem_ld32(tO + c * 32, tt);
       if (store) {
 #pragma unroll
         for (int i = 0; i < 32; i += 4)
           *reinterpret_cast<float4*>(orow + c * 32 + i) =
-              make_float4(t[i] * inv, t[i + 1] * inv, t[i + 2] * inv, t[i + 3] * inv);
+              make_float4(tt[i] * inv, tt[i + 1] * inv, tt[i + 2] * inv, tt[i + 3] * inv);
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 4 * NT + 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, 256 * NT);
   }
 }
 
@@ -435,12 +502,15 @@ bool encode_f16_rows(CUtensorMap* map, const void* base, int64_t width, int64_t 
   return true;
 }
 
-template <int HD>
-int launch_hd(const PrefillArgs& a, int grid, cudaStream_t stream, std::string* err) {
-  const size_t smem = PrefillSmem<HD>::kBytes + 1024;
-  cudaFuncSetAttribute(prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+template <int HD, int NT>
+int launch_hd(PrefillArgs a, cudaStream_t stream, std::string* err) {
+  using SM = PrefillSmem<HD, NT>;
+  const size_t smem = SM::kBytes + 1024;
+  a.n_qblocks = (a.L + kBM * NT - 1) / (kBM * NT);
+  const int grid = a.n_qblocks * a.n_heads;
+  cudaFuncSetAttribute(prefill_kernel<HD, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)smem);
-  prefill_kernel<HD><<<grid, kThreads, smem, stream>>>(a);
+  prefill_kernel<HD, NT><<<grid, SM::kThreads, smem, stream>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     *err = std::string("prefill launch failed: ") + cudaGetErrorString(e);
@@ -459,9 +529,10 @@ int launch_prefill_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
     *err = "prefill head_dim must be 64, 96 or 128";
     return GLA_ERR_NOT_SUPPORTED;
   }
-  const size_t need = (head_dim == 64    ? PrefillSmem<64>::kBytes
-                       : head_dim == 96 ? PrefillSmem<96>::kBytes
-                                        : PrefillSmem<128>::kBytes) +
+  // two 128-row query tiles per CTA where shared memory allows, one otherwise
+  const size_t need = (head_dim == 64    ? PrefillSmem<64, 2>::kBytes
+                       : head_dim == 96 ? PrefillSmem<96, 2>::kBytes
+                                        : PrefillSmem<128, 1>::kBytes) +
                       1024;
   if (need > (size_t)dev.smem_optin) {
     *err = "prefill shared memory layout does not fit";
@@ -481,14 +552,12 @@ int launch_prefill_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
   a.L = L;
   a.n_heads = n_heads;
   a.kv_mul = n_heads / n_kv_heads;
-  a.n_qblocks = (L + kBM - 1) / kBM;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.status = status;
-  const int grid = a.n_qblocks * n_heads;
   switch (head_dim) {
-    case 64: return launch_hd<64>(a, grid, stream, err);
-    case 96: return launch_hd<96>(a, grid, stream, err);
-    default: return launch_hd<128>(a, grid, stream, err);
+    case 64: return launch_hd<64, 2>(a, stream, err);
+    case 96: return launch_hd<96, 2>(a, stream, err);
+    default: return launch_hd<128, 1>(a, stream, err);
   }
 }
 
