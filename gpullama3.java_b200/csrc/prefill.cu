@@ -38,6 +38,11 @@ namespace {
 constexpr int kBM = 128;       // query rows per CTA
 constexpr int kBN = 128;       // keys per block
 constexpr float kRescaleLog2 = 8.0f;
+// Pairs of every 4 (per 8 keys) whose exponentials use the FMA-pipe
+// polynomial instead of MUFU.  Measured on B200: the softmax is issue-bound,
+// so moving work off MUFU costs more than it saves (0 of 4: 600 TFLOP/s,
+// 2 of 4: 549 TFLOP/s on config 5).
+constexpr int kPolyPairs = 0;
 
 struct PrefillArgs {
   CUtensorMap tq;  // [L][n_heads*hd]    box (32, 128), SWIZZLE_64B
@@ -117,6 +122,70 @@ __device__ __forceinline__ void tmem_ld128(uint32_t taddr, float (&v)[128]) {
   for (int i = 0; i < 128; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Half a row (64 columns) in one load + wait.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---- packed FP32 pairs (sm_100 f32x2 instructions) -----------------------
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair on the FMA pipe (takes load off the MUFU unit, which the
+// softmax otherwise saturates).  Cody-Waite split x = n + f with n the
+// nearest integer (the 1.5*2^23 shifter leaves n in the low mantissa bits)
+// and f in [-1/2, 1/2]; 2^f from a degree-4 polynomial fitted to 2^f at
+// Chebyshev nodes by iteratively reweighted least squares (max relative
+// error 2.7e-6 in FP32, below FP16 rounding of P); n is added to the
+// exponent field as an integer.  Inputs are clamped to >= -126, so a masked
+// score (-inf) gives ~1e-38 instead of 0, which FP16 P rounds to 0.
+constexpr float kE2C0 = 0x1.ffffe8p-1f, kE2C1 = 0x1.62e0dcp-1f, kE2C2 = 0x1.ec06dap-3f,
+                kE2C3 = 0x1.ca1440p-5f, kE2C4 = 0x1.3997d4p-7f;
+__device__ __forceinline__ void exp2_poly_pair(float x0, float x1, float& y0, float& y1) {
+  const float kShift = 12582912.0f;  // 1.5 * 2^23
+  const uint64_t X = pk2(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t T = add2(X, pk2(kShift, kShift));
+  const uint64_t N = add2(T, pk2(-kShift, -kShift));
+  const uint64_t F = fma2(N, pk2(-1.f, -1.f), X);
+  uint64_t P = fma2(pk2(kE2C4, kE2C4), F, pk2(kE2C3, kE2C3));
+  P = fma2(P, F, pk2(kE2C2, kE2C2));
+  P = fma2(P, F, pk2(kE2C1, kE2C1));
+  P = fma2(P, F, pk2(kE2C0, kE2C0));
+  float p0, p1, t0, t1;
+  upk2(P, p0, p1);
+  upk2(T, t0, t1);
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
 // 2^x on the MUFU unit (flush-to-zero: subnormal probabilities become 0).
 __device__ __forceinline__ float ex2_ftz(float x) {
   float y;
@@ -193,7 +262,7 @@ struct PrefillSmem {
   static constexpr int kNumBars = 1 + 2 * kKS + 2 * kVS + 4 * NT + 1;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 32;
-  static constexpr int kThreads = (4 * NT + 2) * 32;
+  static constexpr int kThreads = (4 * NT + 2) * 32;  // softmax warpgroups + producer + MMA
 };
 
 // NT query tiles of 128 rows per CTA share every K/V block; tile t has its own
@@ -203,8 +272,9 @@ struct PrefillSmem {
 // other tile's softmax works.
 template <int HD, int NT>
 __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
-    __maxnreg__(NT == 2 ? 200 : 232) prefill_kernel(const __grid_constant__ PrefillArgs a) {
+    prefill_kernel(const __grid_constant__ PrefillArgs a) {
   using SM = PrefillSmem<HD, NT>;
+
   constexpr int KS = SM::kKS, VS = SM::kVS;
   extern __shared__ __align__(1024) char smem_raw[];
   char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -357,7 +427,7 @@ __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
       mbar_wait(mma_done, 0, &no_abort, a.status);
       (void)ok;
     }
-  } else {
+  } else if (warp < 4 * NT) {
     // ------------------------------------------------------------- softmax
     const int t = warp >> 2;                  // query tile of this warpgroup
     const int r = tid & 127;                  // row inside the tile (== TMEM lane)
@@ -375,27 +445,28 @@ __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
     for (int j = 0; j < nb; ++j) {
       mbar_wait(&s_full[t], (uint32_t)(j & 1), abort_flag, a.status);
       tc_fence_after();
-      float s[kBN];
-      tmem_ld128(tS, s);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[t]);
-      // row max of the raw scores (4 independent chains); the causal mask
-      // only touches the diagonal block
-      if (j == qt) {
-#pragma unroll
-        for (int c = 0; c < kBN; ++c)
-          if (j * kBN + c > qi) s[c] = -INFINITY;
-      }
+      // pass 1: row max of the raw scores, two 64-column halves (4 chains);
+      // the causal mask only touches the diagonal block
+      const bool diag = (j == qt);
       float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < kBN; c += 4) {
-        m4[0] = fmaxf(m4[0], s[c]);
-        m4[1] = fmaxf(m4[1], s[c + 1]);
-        m4[2] = fmaxf(m4[2], s[c + 2]);
-        m4[3] = fmaxf(m4[3], s[c + 3]);
+      for (int hh = 0; hh < 2; ++hh) {
+        float s[64];
+        tmem_ld64(tS + hh * 64, s);
+        if (diag) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (j * kBN + hh * 64 + c > qi) s[c] = -INFINITY;
+        }
+#pragma unroll
+        for (int c = 0; c < 64; c += 8) {
+          m4[0] = max3(m4[0], s[c], s[c + 1]);
+          m4[1] = max3(m4[1], s[c + 2], s[c + 3]);
+          m4[2] = max3(m4[2], s[c + 4], s[c + 5]);
+          m4[3] = max3(m4[3], s[c + 6], s[c + 7]);
+        }
       }
-      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;
+      const float mx = max3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * sl2;
       // P_t(j-1) and O_t: wait until P_t(j-1) V_{j-1} has finished
       if (j > 0) {
         mbar_wait(&pdone[t], (uint32_t)((j - 1) & 1), abort_flag, a.status);
@@ -419,23 +490,49 @@ __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
         }
         tmem_wait_st();
       }
-      // p = 2^(s - m_ref) <= 2^8, FP16 into the swizzled P buffer of the tile
-      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+      // pass 2: p = 2^(s - m_ref) <= 2^8, FP16 into the swizzled P buffer;
+      // per 8 keys kPolyPairs pairs use the FMA-pipe polynomial, the rest MUFU
+      uint64_t rsum = pk2(0.f, 0.f);
+      const uint64_t SL = pk2(sl2, sl2), NM = pk2(-m_ref, -m_ref);
 #pragma unroll
-      for (int ch = 0; ch < kBN / 8; ++ch) {  // 16-byte chunks of 8 keys
-        uint32_t w[4];
+      for (int hh = 0; hh < 2; ++hh) {
+        float s[64];
+        tmem_ld64(tS + hh * 64, s);
+        if (diag) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2_ftz(fmaf(s[ch * 8 + 2 * e], sl2, -m_ref));
-          const float p1 = ex2_ftz(fmaf(s[ch * 8 + 2 * e + 1], sl2, -m_ref));
-          rs4[e] += p0 + p1;
-          const __half2 hp = __floats2half2_rn(p0, p1);
-          w[e] = *reinterpret_cast<const uint32_t*>(&hp);
+          for (int c = 0; c < 64; ++c)
+            if (j * kBN + hh * 64 + c > qi) s[c] = -INFINITY;
         }
-        const uint32_t off = sw64_off(kBM, ch >> 2, r, ch & 3);
-        *reinterpret_cast<uint4*>(pb + off) = make_uint4(w[0], w[1], w[2], w[3]);
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {  // 16-byte chunks of 8 keys
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint64_t X = fma2(pk2(s[ch * 8 + 2 * e], s[ch * 8 + 2 * e + 1]), SL, NM);
+            float x0, x1, p0, p1;
+            upk2(X, x0, x1);
+            if (e < kPolyPairs) {
+              exp2_poly_pair(x0, x1, p0, p1);
+            } else {
+              p0 = ex2_ftz(x0);
+              p1 = ex2_ftz(x1);
+            }
+            rsum = add2(rsum, pk2(p0, p1));
+            const __half2 hp = __floats2half2_rn(p0, p1);
+            w[e] = *reinterpret_cast<const uint32_t*>(&hp);
+          }
+          const int cg = hh * 8 + ch;  // chunk of the 128-key row
+          const uint32_t off = sw64_off(kBM, cg >> 2, r, cg & 3);
+          *reinterpret_cast<uint4*>(pb + off) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
       }
-      l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+      float rs0, rs1;
+      upk2(rsum, rs0, rs1);
+      // S_t(j) has been read: the MMA may overwrite it with S_t(j+1)
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[t]);
+      l += rs0 + rs1;
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
