@@ -30,6 +30,7 @@ struct gla_ctx {
   float* gathered = nullptr;        // sharded decode: all ranks' records
   size_t records_cap = 0;           // floats per rank
   gla::Comm comm;
+  int32_t opt_early_kv = 1;         // GLA_OPT_EARLY_KV_PREFETCH
   std::string last_error;
 };
 
@@ -151,6 +152,7 @@ int decode_single(gla_ctx* ctx, int dtype, const float* q, const void* k, const 
   req.scale = scale;
   req.out = out;
   req.record_mode = record_mode;
+  req.early_kv = ctx->opt_early_kv;
   return run_decode(ctx, req);
 }
 
@@ -384,6 +386,17 @@ int32_t gla_reserve(gla_ctx* ctx, int32_t max_batch, int32_t max_kv_heads, int32
 
 int32_t gla_num_sms(const gla_ctx* ctx) { return ctx ? ctx->dev.sms : 0; }
 
+int32_t gla_set_option(gla_ctx* ctx, int32_t option, int32_t value) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  switch (option) {
+    case GLA_OPT_EARLY_KV_PREFETCH:
+      ctx->opt_early_kv = value ? 1 : 0;
+      return GLA_OK;
+    default:
+      return fail(ctx, GLA_ERR_INVALID_ARG, "unknown option");
+  }
+}
+
 int32_t gla_kv_cache_alloc(gla_ctx* ctx, int32_t n_layers, int32_t context_length, int32_t kv_dim,
                            int32_t dtype, void** key_cache, void** value_cache) {
   if (!ctx || !key_cache || !value_cache) return GLA_ERR_INVALID_ARG;
@@ -569,38 +582,41 @@ int32_t gla_rope_append_f32(gla_ctx* ctx, float* q, float* k, const float* v, fl
 }
 
 int64_t gla_debug_partition(const int32_t* n_pos, int32_t n_seq, int32_t n_kv_heads, int32_t tile,
-                            int32_t n_ctas, int32_t* cta, int32_t* seq, int32_t* kv_head,
-                            int32_t* row0, int32_t* slot, int64_t capacity) {
-  if (!n_pos || n_seq < 1 || n_kv_heads < 1 || tile < 1 || n_ctas < 1)
+                            int32_t unit_rows, int32_t n_ctas, int32_t* cta, int32_t* seq,
+                            int32_t* kv_head, int32_t* row0, int32_t* rows, int32_t* slot,
+                            int64_t capacity) {
+  if (!n_pos || n_seq < 1 || n_kv_heads < 1 || n_ctas < 1 || unit_rows < 1 || tile < unit_rows ||
+      tile % unit_rows != 0)
     return GLA_ERR_INVALID_ARG;
-  std::vector<int32_t> ntiles(n_seq), start(n_seq + 1);
+  std::vector<int32_t> nunits(n_seq), start(n_seq + 1), np(n_seq);
   int64_t acc = 0;
   for (int b = 0; b < n_seq; ++b) {
-    int32_t np = n_pos[b] < 0 ? 0 : n_pos[b];
-    ntiles[b] = gla::ceil_div(np, tile);
+    np[b] = n_pos[b] < 0 ? 0 : n_pos[b];
+    nunits[b] = gla::ceil_div(np[b], unit_rows);
     start[b] = (int32_t)(acc * n_kv_heads);
-    acc += ntiles[b];
+    acc += nunits[b];
   }
   start[n_seq] = (int32_t)(acc * n_kv_heads);
-  const int32_t W = start[n_seq];
-  if (W > capacity) return GLA_ERR_INVALID_ARG;
-  const gla::Split sp = gla::make_split(W, n_ctas);
-  // walk each CTA's range exactly as the kernel's producer/consumers do
+  const gla::Split sp = gla::make_split(start[n_seq], n_ctas);
+  // walk each CTA's range exactly as the kernel's producer and consumers do
+  int64_t n = 0;
   for (int32_t c = 0; c < n_ctas; ++c) {
     const int32_t lo = gla::split_lo(sp, c), cnt = gla::split_count(sp, c);
-    if (cnt == 0) continue;
-    gla::TileRef tr = gla::locate_tile(start.data(), ntiles.data(), n_seq, n_kv_heads, lo);
-    for (int32_t i = 0; i < cnt; ++i) {
-      const int32_t t = lo + i;
-      cta[t] = c;
-      seq[t] = tr.b;
-      kv_head[t] = tr.g;
-      row0[t] = tr.j * tile;
-      slot[t] = c + tr.b * n_kv_heads + tr.g;
-      gla::next_tile(tr, ntiles.data(), n_seq, n_kv_heads);
+    gla::TileWalk wk;
+    wk.init(start.data(), nunits.data(), n_seq, lo, lo + cnt);
+    gla::Tile t;
+    while (wk.next(nunits.data(), n_seq, n_kv_heads, tile / unit_rows, unit_rows, t)) {
+      if (n >= capacity) return GLA_ERR_INVALID_ARG;
+      cta[n] = c;
+      seq[n] = t.b;
+      kv_head[n] = t.g;
+      row0[n] = t.row0;
+      rows[n] = std::min(t.units * unit_rows, np[t.b] - t.row0);
+      slot[n] = c + t.b * n_kv_heads + t.g;
+      ++n;
     }
   }
-  return W;
+  return n;
 }
 
 }  // extern "C"

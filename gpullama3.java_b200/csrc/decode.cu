@@ -3,6 +3,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <mutex>
 
@@ -13,8 +14,10 @@ namespace gla {
 
 namespace {
 
-constexpr int kNW = 4;  // consumer warps (both consumers)
 constexpr int kTileMax = 64;
+
+// consumer warps: FP32 F32Consumer (8), FP16 F16Consumer (4)
+int nw_for(int dtype) { return dtype == GLA_DTYPE_F32 ? 8 : 4; }
 constexpr int kMaxStages = 8;
 
 size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
@@ -27,12 +30,12 @@ int esize_for(int dtype) { return dtype == GLA_DTYPE_F32 ? 4 : 2; }
 
 int group_cap_for(int dtype, int group) {
   if (dtype == GLA_DTYPE_F16) return kMaxGroup;
-  return group <= 1 ? 1 : group <= 2 ? 2 : group <= 4 ? 4 : 8;
+  return group <= 4 ? group : 8;
 }
 
 // Shared memory layout for a given tile/stage count.
 struct Layout {
-  int32_t off_bars, off_seq, off_q, off_pbuf, off_merge, off_comb, off_flags;
+  int32_t off_bars, off_seq, off_q, off_pbuf, off_merge, off_flags;
   size_t total;
 };
 
@@ -46,12 +49,13 @@ Layout layout_for(int dtype, int hd, int group, int tile, int stages, int batch,
   L.off_q = (int32_t)align16(off);
   off = L.off_q + (size_t)kMaxGroup * hd * sizeof(float);
   L.off_pbuf = (int32_t)align16(off);
-  off = L.off_pbuf + (dtype == GLA_DTYPE_F16 ? 0 : (size_t)kNW * 16 * 8 * sizeof(float));
+  const int nw = nw_for(dtype);
+  off = L.off_pbuf +
+        (dtype == GLA_DTYPE_F16 ? 0 : (size_t)nw * F32Consumer<128, 1>::kPbufFloats * sizeof(float));
   L.off_merge = (int32_t)align16(off);
-  off = L.off_merge + (size_t)kNW * group_cap_for(dtype, group) * (hd + 2) * sizeof(float);
-  L.off_comb = (int32_t)align16(off);
-  off = L.off_comb + (size_t)(2 * grid + 2) * kMaxGroup * sizeof(float);
+  off = L.off_merge + (size_t)nw * group_cap_for(dtype, group) * (hd + 2) * sizeof(float);
   L.off_flags = (int32_t)align16(off);
+  (void)grid;
   L.total = L.off_flags + 16 + 1024;  // + slack to 1024-align the stage ring
   return L;
 }
@@ -87,6 +91,7 @@ cudaError_t launch_f32(const DecodeArgs& a, const DecodePlan& p, cudaStream_t st
   switch (group_cap_for(GLA_DTYPE_F32, a.group)) {
     case 1: return launch_impl<HD, F32Consumer<HD, 1>, LOADER>(a, p, st);
     case 2: return launch_impl<HD, F32Consumer<HD, 2>, LOADER>(a, p, st);
+    case 3: return launch_impl<HD, F32Consumer<HD, 3>, LOADER>(a, p, st);
     case 4: return launch_impl<HD, F32Consumer<HD, 4>, LOADER>(a, p, st);
     default: return launch_impl<HD, F32Consumer<HD, 8>, LOADER>(a, p, st);
   }
@@ -171,12 +176,13 @@ int plan_decode(const DecodeRequest& r, const DeviceInfo& dev, DecodePlan* p, st
     *err = "batch must be in [1, 1024]";
     return GLA_ERR_NOT_SUPPORTED;
   }
-  // Tile: largest tile that still gives every SM at least two tiles.
+  // Work is streamed and dealt to CTAs in whole tiles of kTileMax rows.
+  // (16-row units, balanced to +-16 rows per CTA, measured slower on B200
+  // for every decode shape tried, 512 to 128K rows: the extra pieces and
+  // ragged boxes cost more than the imbalance of one tile.)
   const int64_t rows = std::max<int64_t>(1, r.max_n_pos);
-  int tile = kTileMax;
-  auto tiles_at = [&](int t) { return (int64_t)r.batch * r.n_kv * ((rows + t - 1) / t); };
-  while (tile > 16 && tiles_at(tile) < 2 * (int64_t)dev.sms) tile >>= 1;
-  const int64_t W = tiles_at(tile);
+  const int tile = kTileMax;
+  const int64_t W = (int64_t)r.batch * r.n_kv * ((rows + tile - 1) / tile);
   if (W > (int64_t)1 << 30) {
     *err = "decode work too large for one call";
     return GLA_ERR_NOT_SUPPORTED;
@@ -199,7 +205,7 @@ int plan_decode(const DecodeRequest& r, const DeviceInfo& dev, DecodePlan* p, st
   p->tile = tile;
   p->stages = stages;
   p->grid = grid;
-  p->threads = (kNW + 1) * 32;
+  p->threads = (nw_for(r.dtype) + 1) * 32;
   p->smem = L.total;
   p->part_floats = (size_t)(grid + r.batch * r.n_kv) * group * (hd + 4);
   p->counters = (size_t)r.batch * r.n_kv;
@@ -228,6 +234,7 @@ int launch_decode(const DecodeRequest& r, const DecodePlan& p, float* ws_part, i
   a.n_pos = r.n_pos;
   a.n_pos_add = r.n_pos_add;
   a.n_pos_cap = r.n_pos_cap;
+  a.early_kv = r.early_kv;
   a.batch = r.batch;
   a.n_heads = r.n_heads;
   a.n_kv = r.n_kv;
@@ -246,7 +253,6 @@ int launch_decode(const DecodeRequest& r, const DecodePlan& p, float* ws_part, i
   a.off_pbuf = L.off_pbuf;
   a.off_q = L.off_q;
   a.off_merge = L.off_merge;
-  a.off_comb = L.off_comb;
   a.off_flags = L.off_flags;
   cudaError_t rc = loader == 0 ? launch_any<0>(r.dtype, hd, a, p, stream)
                                 : launch_any<1>(r.dtype, hd, a, p, stream);

@@ -41,7 +41,7 @@
 namespace gla {
 
 struct DecodeArgs {
-  CUtensorMap tmap_k;          // LOADER 0: [rows][kv_stride] box (col_block, tile)
+  CUtensorMap tmap_k;          // LOADER 0: [rows][kv_stride] box (col_block, tile rows)
   CUtensorMap tmap_v;
   const float* q;              // [B][n_heads][HD]
   const void* k;               // layer base (single sequence) or nullptr
@@ -54,11 +54,13 @@ struct DecodeArgs {
   int32_t n_pos_add;           // added to n_pos_dev[b] (position holder: +1)
   int32_t n_pos_cap;           // rows present in the cache; larger n_pos is clamped
                                // and latched as GLA_ERR_INVALID_ARG
+  int32_t early_kv;            // LOADER 0, host n_pos: prefetch history tiles before
+                               // the preceding grid completes (see kernel)
   int32_t batch;
   int32_t n_heads;
   int32_t n_kv;
   int32_t group;               // G
-  int32_t tile;                // rows per stage
+  int32_t tile;                // rows per stage and per work unit
   int32_t stages;
   float q_scale;               // scale * log2(e)
   float* out;                  // xb [B][n_heads][HD] or records [B][n_heads][HD+2]
@@ -73,7 +75,6 @@ struct DecodeArgs {
   int32_t off_pbuf;
   int32_t off_q;               // the group's q vectors [kMaxGroup][HD]
   int32_t off_merge;
-  int32_t off_comb;            // combine scratch: m/l per (piece, head), M/L per head
   int32_t off_flags;
 };
 
@@ -108,122 +109,169 @@ struct TileLayout {
 };
 
 // ---------------------------------------------------------------------------
-// FP32 cache consumer (CUDA-core FMA; an FP32 cache delivers at most G/2 FLOP
-// per byte).  Each warp owns 16 rows of a tile.
-//   phase A (q.k): lane = (row, half of head_dim); the lane streams its
-//     row's K chunks and multiplies them with the G q vectors, broadcast from
-//     shared memory; one shuffle joins the two halves.
-//   online softmax: one 16-row max per head per tile.
-//   phase B (p.v): lane = 1/32 of head_dim; rows are accumulated in turn.
+// FP32 cache consumer (CUDA-core FMA; an FP32 cache carries at most G/2 FLOP
+// per byte).  8 warps, each owning 8 rows of a tile (two warps per scheduler
+// hide each other's latency).  Latency bounds it, and a consumer squeezed
+// below the 168 registers that 9 warps allow serialises its loads, so the
+// layout keeps q small in registers and every load batch independent.
+//   phase A (q.k): lane = (row rl of kRL, part of kLP = 32/kRL): the lane
+//     streams kEC = head_dim/(4 kLP) float4 chunks of its row against the
+//     same chunks of the G q vectors (registers while they take <= 64 of
+//     them, else shared memory); hd >= 96 uses 4 rows x 8 parts, two passes
+//     over the warp's 8 rows, hd 64 uses 8 rows x 4 parts.  Shuffles over
+//     the parts join the dot products.
+//   online softmax: one 8-row max per head per tile, branch-free so the G
+//     heads' shuffle chains interleave (a lazy, vote-guarded rescale measured
+//     slower: the branches serialise the heads).
+//   phase B (p.v): lane = one float4 column chunk (two rows per pass when a
+//     row has 16 chunks); all 8 rows unrolled, p read back as one float4 per
+//     row and 4 heads; rows past the tile's end contribute zero (their V is
+//     not trusted: it may be stale cache memory).
 // ---------------------------------------------------------------------------
 template <int HD, int GT>
 struct F32Consumer {
   using TL = TileLayout<4, HD>;
   static constexpr int kElemBytes = 4;
-  static constexpr int kNW = 4;
-  static constexpr int kTileMax = 16 * kNW;
+  static constexpr int kNW = 8;
+  static constexpr int kRows = 8;               // rows per warp
+  static constexpr int kTileMax = kRows * kNW;  // 64
   static constexpr int kMergeG = GT;
-  static constexpr int kPbufFloats = 16 * 8;  // per warp: 16 rows x 8 heads
-  static constexpr int kChunks = HD / 4;      // float4 chunks per row
-  static constexpr int kHalf = kChunks / 2;   // phase A chunks per lane
-  static constexpr int kVB = HD / 32;         // phase B floats per lane
+  static constexpr int kPbufFloats = kRows * 8;  // per warp: 8 rows x 8 heads
+  static constexpr int kC4 = HD / 4;             // float4 chunks per row
+  static constexpr int kLP = HD >= 96 ? 8 : 4;   // phase A lanes per row
+  static constexpr int kRL = 32 / kLP;           // phase A rows per pass
+  static constexpr int kPA = kRows / kRL;        // phase A passes
+  static constexpr int kEC = kC4 / kLP;          // phase A chunks per lane and row
+  static constexpr int kRPP = (32 % kC4 == 0) ? 32 / kC4 : 1;  // phase B rows per pass
+  static constexpr int kPasses = kRows / kRPP;
+  static constexpr int kPH = (GT + 3) / 4;       // float4s of p per row
+  static constexpr bool kQReg = GT * kEC * 4 <= 64;
+  static_assert(kC4 % kLP == 0, "head_dim must be a multiple of 16 (32 from 96 up)");
+  static_assert(kRPP <= 2, "phase B covers at most two rows per pass");
 
-  float m[GT], l[GT];  // m: warp-uniform; l: per-lane part (lanes 0-15 own rows)
-  float o[GT][kVB];
+  float m[GT], l[GT];  // m: warp-uniform; l: per-lane part (part-0 lanes own rows)
+  float4 o[GT];        // phase B chunk of each head (half sums when kRPP == 2)
+  float4 qr[kQReg ? GT : 1][kQReg ? kEC : 1];
 
-  __device__ __forceinline__ void begin(const DecodeArgs&, const float*, int) {
+  __device__ __forceinline__ void begin(const DecodeArgs&, const float* qs, int lane) {
 #pragma unroll
     for (int h = 0; h < GT; ++h) {
       m[h] = -INFINITY;
       l[h] = 0.f;
+      o[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if constexpr (kQReg) {
+      const int part = lane / kRL;
 #pragma unroll
-      for (int e = 0; e < kVB; ++e) o[h][e] = 0.f;
+      for (int h = 0; h < GT; ++h)
+#pragma unroll
+        for (int i = 0; i < kEC; ++i)
+          qr[h][i] = *reinterpret_cast<const float4*>(qs + h * HD + (part * kEC + i) * 4);
     }
   }
 
   __device__ __forceinline__ void consume(const DecodeArgs& a, const char* stage, int rows,
                                           float* pbuf_w, const float* qs, int w, int lane) {
-    const int rb = w * 16;
+    const int rb = w * kRows;
     if (rb >= rows) return;
-    const int rl = lane & 15, half = lane >> 4;
-    const int row = rb + rl;
+    const int rl = lane % kRL, part = lane / kRL;
     const char* Ks = stage;
     const char* Vs = stage + a.tile * HD * 4;
-    float acc[GT];
+    float acc[kPA][GT];
 #pragma unroll
-    for (int h = 0; h < GT; ++h) acc[h] = 0.f;
+    for (int pa = 0; pa < kPA; ++pa)
 #pragma unroll
-    for (int i = 0; i < kHalf; ++i) {
-      const int c = half * kHalf + i;
-      const float4 k4 = *reinterpret_cast<const float4*>(Ks + TL::chunk_off(a.tile, row, c * 4));
+      for (int h = 0; h < GT; ++h) acc[pa][h] = 0.f;
+#pragma unroll
+    for (int i = 0; i < kEC; ++i) {
+      const int c = part * kEC + i;
+      float4 k4[kPA];
+#pragma unroll
+      for (int pa = 0; pa < kPA; ++pa)
+        k4[pa] = *reinterpret_cast<const float4*>(Ks + TL::chunk_off(a.tile, rb + pa * kRL + rl, c * 4));
 #pragma unroll
       for (int h = 0; h < GT; ++h) {
-        const float4 q4 = *reinterpret_cast<const float4*>(qs + h * HD + c * 4);
-        acc[h] = fmaf(q4.x, k4.x, acc[h]);
-        acc[h] = fmaf(q4.y, k4.y, acc[h]);
-        acc[h] = fmaf(q4.z, k4.z, acc[h]);
-        acc[h] = fmaf(q4.w, k4.w, acc[h]);
+        float4 q4;
+        if constexpr (kQReg) q4 = qr[h][i];
+        else q4 = *reinterpret_cast<const float4*>(qs + h * HD + c * 4);
+#pragma unroll
+        for (int pa = 0; pa < kPA; ++pa) {
+          float& ac = acc[pa][h];
+          ac = fmaf(q4.x, k4[pa].x, ac);
+          ac = fmaf(q4.y, k4[pa].y, ac);
+          ac = fmaf(q4.z, k4[pa].z, ac);
+          ac = fmaf(q4.w, k4[pa].w, ac);
+        }
       }
     }
-    const bool valid = row < rows;
-    float p[GT];
+    float p[kPA][kPH * 4];
 #pragma unroll
     for (int h = 0; h < GT; ++h) {
-      const float sc = acc[h] + __shfl_xor_sync(0xffffffffu, acc[h], 16);
-      const float s = valid ? sc : -INFINITY;
-      float mt = s;
+      float sv[kPA];
+      float mt = -INFINITY;
 #pragma unroll
-      for (int off = 8; off >= 1; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+      for (int pa = 0; pa < kPA; ++pa) {
+        float sc = acc[pa][h];
+#pragma unroll
+        for (int off = kRL; off < 32; off <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off);
+        sv[pa] = (rb + pa * kRL + rl < rows) ? sc : -INFINITY;
+        mt = fmaxf(mt, sv[pa]);
+      }
+#pragma unroll
+      for (int off = 1; off < kRL; off <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
       const float mn = fmaxf(m[h], mt);  // finite: row rb is valid
       const float alpha = fast_exp2(m[h] - mn);
-      p[h] = fast_exp2(s - mn);
-      l[h] = l[h] * alpha + (half == 0 ? p[h] : 0.f);
+      float ps = 0.f;
+#pragma unroll
+      for (int pa = 0; pa < kPA; ++pa) {
+        p[pa][h] = fast_exp2(sv[pa] - mn);
+        ps += p[pa][h];
+      }
+      l[h] = l[h] * alpha + (part == 0 ? ps : 0.f);
       m[h] = mn;
-#pragma unroll
-      for (int e = 0; e < kVB; ++e) o[h][e] *= alpha;
+      o[h].x *= alpha;
+      o[h].y *= alpha;
+      o[h].z *= alpha;
+      o[h].w *= alpha;
     }
-    if (half == 0) {
-      float* pr = pbuf_w + rl * 8;
+    if (part == 0) {
 #pragma unroll
-      for (int h = 0; h < GT; ++h) pr[h] = p[h];
+      for (int pa = 0; pa < kPA; ++pa) {
+#pragma unroll
+        for (int h = GT; h < kPH * 4; ++h) p[pa][h] = 0.f;
+        float4* pr = reinterpret_cast<float4*>(pbuf_w + (pa * kRL + rl) * 8);
+#pragma unroll
+        for (int u = 0; u < kPH; ++u)
+          pr[u] = make_float4(p[pa][4 * u], p[pa][4 * u + 1], p[pa][4 * u + 2], p[pa][4 * u + 3]);
+      }
     }
     __syncwarp();
-    const int nrows = min(16, rows - rb);
-    for (int r = 0; r < nrows; ++r) {
-      const int vrow = rb + r;
-      float vv[kVB];
-      if constexpr (kVB == 4) {
-        const float4 t = *reinterpret_cast<const float4*>(Vs + TL::chunk_off(a.tile, vrow, lane * 4));
-        vv[0] = t.x; vv[1] = t.y; vv[2] = t.z; vv[3] = t.w;
-      } else if constexpr (kVB == 2) {
-        const int d = lane * 2;
-        const float2 t = *reinterpret_cast<const float2*>(
-            Vs + TL::chunk_off(a.tile, vrow, d & ~3) + (d & 3) * 4);
-        vv[0] = t.x; vv[1] = t.y;
-      } else {
+    const int nvalid = rows - rb;
+    const int sub = kRPP > 1 ? lane / kC4 : 0;
+    const int ch = kRPP > 1 ? lane % kC4 : imin(lane, kC4 - 1);  // lanes >= kC4 idle (hd 96)
+    const bool lane_on = kRPP > 1 || lane < kC4;
 #pragma unroll
-        for (int e = 0; e < kVB; ++e) {
-          const int d = lane * kVB + e;
-          vv[e] = *reinterpret_cast<const float*>(Vs + TL::chunk_off(a.tile, vrow, d & ~3) +
-                                                  (d & 3) * 4);
+    for (int j = 0; j < kPasses; ++j) {
+      const int r = j * kRPP + sub;
+      const float4 t = *reinterpret_cast<const float4*>(Vs + TL::chunk_off(a.tile, rb + r, ch * 4));
+      const bool ok = lane_on && r < nvalid;
+      const float4 vv = ok ? t : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4* pr = reinterpret_cast<const float4*>(pbuf_w + r * 8);
+#pragma unroll
+      for (int u = 0; u < kPH; ++u) {
+        const float4 pu = pr[u];
+        const float pw[4] = {pu.x, pu.y, pu.z, pu.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int h = 4 * u + e;
+          if (h < GT) {
+            o[h].x = fmaf(pw[e], vv.x, o[h].x);
+            o[h].y = fmaf(pw[e], vv.y, o[h].y);
+            o[h].z = fmaf(pw[e], vv.z, o[h].z);
+            o[h].w = fmaf(pw[e], vv.w, o[h].w);
+          }
         }
       }
-      const float* prow = pbuf_w + r * 8;
-      float pr[GT];
-      if constexpr (GT >= 4) {
-#pragma unroll
-        for (int h4 = 0; h4 < GT; h4 += 4) {
-          const float4 t = *reinterpret_cast<const float4*>(prow + h4);
-          pr[h4] = t.x; pr[h4 + 1] = t.y; pr[h4 + 2] = t.z; pr[h4 + 3] = t.w;
-        }
-      } else {
-#pragma unroll
-        for (int h = 0; h < GT; ++h) pr[h] = prow[h];
-      }
-#pragma unroll
-      for (int h = 0; h < GT; ++h)
-#pragma unroll
-        for (int e = 0; e < kVB; ++e) o[h][e] = fmaf(pr[h], vv[e], o[h][e]);
     }
     __syncwarp();
   }
@@ -235,10 +283,21 @@ struct F32Consumer {
       float lt = l[h];
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, off);
+      float4 ov = o[h];
+      if constexpr (kRPP == 2) {
+        ov.x += __shfl_xor_sync(0xffffffffu, ov.x, 16);
+        ov.y += __shfl_xor_sync(0xffffffffu, ov.y, 16);
+        ov.z += __shfl_xor_sync(0xffffffffu, ov.z, 16);
+        ov.w += __shfl_xor_sync(0xffffffffu, ov.w, 16);
+      }
       if (h < a.group) {
         float* mh = merge_w + h * (HD + 2);
-#pragma unroll
-        for (int e = 0; e < kVB; ++e) mh[lane * kVB + e] = o[h][e];
+        if (lane < kC4) {
+          mh[lane * 4 + 0] = ov.x;
+          mh[lane * 4 + 1] = ov.y;
+          mh[lane * 4 + 2] = ov.z;
+          mh[lane * 4 + 3] = ov.w;
+        }
         if (lane == 0) {
           mh[HD] = m[h];
           mh[HD + 1] = lt;
@@ -500,12 +559,14 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   using TL = TileLayout<esize, HD>;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int B = a.batch, n_kv = a.n_kv, G = a.group;
+  const int unit_rows = a.tile;  // work units are whole tiles
+  constexpr int tile_units = 1;
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bars);
   uint64_t* empty = full + a.stages;
-  int32_t* seq_start = reinterpret_cast<int32_t*>(smem + a.off_seq);  // [B+1]
-  int32_t* ntiles = seq_start + (B + 1);                              // [B]
-  int32_t* npos = ntiles + B;                                         // [B]
+  int32_t* seq_start = reinterpret_cast<int32_t*>(smem + a.off_seq);  // [B+1] (units)
+  int32_t* nunits = seq_start + (B + 1);                              // [B]
+  int32_t* npos = nunits + B;                                         // [B]
   float* qs = reinterpret_cast<float*>(smem + a.off_q);                // [kMaxGroup][HD]
   float* pbuf = reinterpret_cast<float*>(smem + a.off_pbuf);           // [NW][kPbufFloats]
   float* merge = reinterpret_cast<float*>(smem + a.off_merge);         // [NW][kMG][HD+2]
@@ -524,39 +585,86 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
     prefetch_tmap(&a.tmap_k);
     prefetch_tmap(&a.tmap_v);
   }
-  // Programmatic dependent launch: everything above only touches shared
-  // memory and kernel parameters; nothing below may read memory a preceding
-  // kernel writes (n_pos, q, caches, the workspace) before that kernel is done.
+  // per-sequence rows and unit prefix (warp 0 scans 32 sequences at a time)
+  auto scan_sequences = [&]() {
+    if (warp == 0) {
+      int32_t carry = 0;
+      for (int base = 0; base < B; base += 32) {
+        const int b = base + lane;
+        int32_t np = 0, nu = 0;
+        if (b < B) {
+          np = a.n_pos_dev ? a.n_pos_dev[b] + a.n_pos_add : a.n_pos;
+          np = np < 0 ? 0 : np;
+          if (np > a.n_pos_cap) {
+            atomicCAS(a.status, 0, GLA_ERR_INVALID_ARG);
+            np = a.n_pos_cap;
+          }
+          nu = ceil_div(np, unit_rows);
+          npos[b] = np;
+          nunits[b] = nu;
+        }
+        int32_t incl = nu;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          int32_t y = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += y;
+        }
+        if (b < B) seq_start[b] = (carry + incl - nu) * n_kv;
+        carry += __shfl_sync(0xffffffffu, incl, 31);
+      }
+      if (lane == 0) seq_start[B] = carry * n_kv;
+    }
+  };
+  // TMA loads of one tile (LOADER 0): whole boxes of `tile` rows; rows past
+  // the tensor map's extent are zero-filled, so the byte count is the boxes'
+  // size.  Rows past n_pos inside the extent are loaded and masked later.
+  auto tma_tile = [&](int st, const Tile& t, uint64_t pol) {
+    char* ks = smem + (size_t)st * a.stage_bytes;
+    char* vs = ks + (size_t)a.tile * HD * esize;
+    mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * a.tile * HD * esize));
+#pragma unroll
+    for (int cb = 0; cb < TL::kBlocks; ++cb) {
+      const int x = t.g * HD + cb * TL::kCW;
+      const size_t off = (size_t)cb * a.tile * TL::kRowB;
+      tma_load_2d(ks + off, &a.tmap_k, x, t.row0, &full[st], pol);
+      tma_load_2d(vs + off, &a.tmap_v, x, t.row0, &full[st], pol);
+    }
+  };
+  // Early KV prefetch (programmatic dependent launch).  With a host n_pos the
+  // work partition needs no memory, so the producer may start streaming this
+  // CTA's first tiles while the preceding kernel on the stream drains.  Only
+  // tiles holding cache history (rows < n_pos - 1) are fetched early: the
+  // newest row is the one a KV append kernel may have just written.  Decode
+  // kernels (the only kernels here that release dependents early) never write
+  // a cache; a preceding kernel that does not release dependents has finished
+  // before this grid starts.
+  const bool early = LOADER == 0 && a.early_kv && a.n_pos_dev == nullptr;
+  int32_t n_early = 0;
+  if (early) {
+    scan_sequences();
+    __syncthreads();
+    if (warp == NW && lane == 0) {
+      const Split sp0 = make_split(seq_start[B], (int32_t)gridDim.x);
+      const int32_t lo = split_lo(sp0, blockIdx.x), cnt = split_count(sp0, blockIdx.x);
+      const uint64_t pol = l2_evict_first_policy();
+      TileWalk wk;
+      wk.init(seq_start, nunits, B, lo, lo + cnt);
+      Tile t;
+      while (n_early < a.stages) {
+        TileWalk probe = wk;
+        if (!probe.next(nunits, B, n_kv, tile_units, unit_rows, t)) break;
+        if (t.row0 + t.units * unit_rows >= npos[t.b]) break;  // holds the newest row
+        wk = probe;
+        tma_tile(n_early, t, pol);
+        ++n_early;
+      }
+    }
+  }
+  // Nothing below may read memory a preceding kernel writes (n_pos, q, the
+  // newest cache rows, the workspace) before that kernel has completed.
   pdl_wait();
   pdl_launch_dependents();
-  // per-sequence rows and tile prefix (warp 0 scans 32 sequences at a time)
-  if (warp == 0) {
-    int32_t carry = 0;
-    for (int base = 0; base < B; base += 32) {
-      const int b = base + lane;
-      int32_t np = 0, nt = 0;
-      if (b < B) {
-        np = a.n_pos_dev ? a.n_pos_dev[b] + a.n_pos_add : a.n_pos;
-        np = np < 0 ? 0 : np;
-        if (np > a.n_pos_cap) {
-          atomicCAS(a.status, 0, GLA_ERR_INVALID_ARG);
-          np = a.n_pos_cap;
-        }
-        nt = ceil_div(np, a.tile);
-        npos[b] = np;
-        ntiles[b] = nt;
-      }
-      int32_t incl = nt;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        int32_t y = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += y;
-      }
-      if (b < B) seq_start[b] = (carry + incl - nt) * n_kv;
-      carry += __shfl_sync(0xffffffffu, incl, 31);
-    }
-    if (lane == 0) seq_start[B] = carry * n_kv;
-  }
+  if (!early) scan_sequences();
   __syncthreads();
 
   const int32_t W = seq_start[B];
@@ -568,33 +676,24 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
     // ---------------- producer ----------------
     if (my_count > 0) {
       const uint64_t pol = l2_evict_first_policy();
-      TileRef tr = locate_tile(seq_start, ntiles, B, n_kv, my_lo);
+      const int32_t first = early ? __shfl_sync(0xffffffffu, n_early, 0) : 0;
+      TileWalk wk;
+      wk.init(seq_start, nunits, B, my_lo, my_lo + my_count);
+      Tile t;
+      for (int32_t k = 0; k < first; ++k) wk.next(nunits, B, n_kv, tile_units, unit_rows, t);
       int cur_b = -1;
       const char* kb = nullptr;
       const char* vb = nullptr;
-      for (int32_t i = 0; i < my_count; ++i) {
-        const int st = i % a.stages;
-        const uint32_t use = (uint32_t)(i / a.stages);
-        if (!mbar_wait(&empty[st], (use & 1u) ^ 1u, flags, a.status)) break;
-        const int row0 = tr.j * a.tile;
-        char* ks = smem + (size_t)st * a.stage_bytes;
-        char* vs = ks + (size_t)a.tile * HD * esize;
+      int st = first % a.stages;
+      uint32_t phase = first < a.stages ? 1u : 0u;  // empty-barrier parity of the ring pass
+      for (; wk.next(nunits, B, n_kv, tile_units, unit_rows, t);) {
+        if (!mbar_wait(&empty[st], phase, flags, a.status)) break;
         if constexpr (LOADER == 0) {
-          // whole boxes, out-of-range rows zero-filled: the byte count is fixed
-          if (lane == 0) {
-            mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * a.tile * HD * esize));
-#pragma unroll
-            for (int cb = 0; cb < TL::kBlocks; ++cb) {
-              const int x = tr.g * HD + cb * TL::kCW;
-              const size_t off = (size_t)cb * a.tile * TL::kRowB;
-              tma_load_2d(ks + off, &a.tmap_k, x, row0, &full[st], pol);
-              tma_load_2d(vs + off, &a.tmap_v, x, row0, &full[st], pol);
-            }
-          }
+          if (lane == 0) tma_tile(st, t, pol);
           __syncwarp();
         } else {
-          if (tr.b != cur_b) {
-            cur_b = tr.b;
+          if (t.b != cur_b) {
+            cur_b = t.b;
             kb = static_cast<const char*>(a.k_ptrs ? a.k_ptrs[cur_b] : a.k);
             vb = static_cast<const char*>(a.v_ptrs ? a.v_ptrs[cur_b] : a.v);
             // caller-supplied device pointers: a null or unaligned base would
@@ -606,19 +705,24 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
               break;
             }
           }
-          const int rows = min(a.tile, npos[tr.b] - row0);
+          char* ks = smem + (size_t)st * a.stage_bytes;
+          char* vs = ks + (size_t)a.tile * HD * esize;
+          const int rows = imin(t.units * unit_rows, npos[t.b] - t.row0);
           constexpr int kCpr = HD * esize / 16;  // 16-byte chunks per row
           for (int idx = lane; idx < rows * kCpr; idx += 32) {
             const int r = idx / kCpr, c = idx - r * kCpr;
             const int64_t off =
-                ((int64_t)(row0 + r) * a.kv_stride + (int64_t)tr.g * HD) * esize + c * 16;
+                ((int64_t)(t.row0 + r) * a.kv_stride + (int64_t)t.g * HD) * esize + c * 16;
             const int soff = TL::chunk_off(a.tile, r, c * (16 / esize));
             cp_async_16(ks + soff, kb + off, pol);
             cp_async_16(vs + soff, vb + off, pol);
           }
           cp_async_arrive_noinc(&full[st]);
         }
-        next_tile(tr, ntiles, B, n_kv);
+        if (++st == a.stages) {
+          st = 0;
+          phase ^= 1u;
+        }
       }
     }
     return;
@@ -628,7 +732,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   // segments with no rows (n_pos <= 0) produce zeros / empty records
   for (int s = blockIdx.x; s < B * n_kv; s += gridDim.x) {
     const int b = s / n_kv, g = s - b * n_kv;
-    if (ntiles[b] == 0)
+    if (nunits[b] == 0)
       for (int idx = tid; idx < G * HD; idx += kNCT)
         write_final<HD>(a, b, g * G + idx / HD, idx % HD, 0.f, 0.f, 0.f);
   }
@@ -637,10 +741,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   Consumer cons;
   float* pbuf_w = pbuf + warp * Consumer::kPbufFloats;
   float* merge_w = merge + warp * kMG * (HD + 2);
-  TileRef tr = locate_tile(seq_start, ntiles, B, n_kv, my_lo);
-  int cur_b = -1, cur_g = -1;
   constexpr int kSH = slot_head_floats<HD>();
-  float* comb = reinterpret_cast<float*>(smem + a.off_comb);  // [2][P][kMaxGroup] + [2][kMaxGroup]
 
   // The group's q vectors, pre-scaled by scale*log2(e), rows >= G zeroed.
   auto load_q = [&](int b, int g) {
@@ -650,75 +751,49 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   };
 
   // Merges the pieces of segment (b, g) held in workspace slots c + s for
-  // c in [c0, c0 + npieces): log-sum-exp weights per (piece, head) first,
-  // then every (head, 4 columns) element with independent float4 loads.
+  // c in [c0, c0 + npieces).  Each thread owns (head, 4 columns) elements and
+  // folds the pieces in with a running log-sum-exp, 16 pieces per round of
+  // loads: no shared memory and no barrier.
   auto combine_pieces = [&](int b, int g, int s, int c0, int npieces) {
-    float* mb = comb;                          // [npieces][kMaxGroup] m, then weights
-    float* lb = comb + gridDim.x * kMaxGroup;  // [npieces][kMaxGroup] l
-    float* MLb = lb + gridDim.x * kMaxGroup;   // M[kMaxGroup], L[kMaxGroup]
-    // (m, l) of every (piece, head): loads issued four deep per thread
-    for (int p0 = 0; p0 < npieces * G; p0 += 4 * kNCT) {
-      float mv[4], lv[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int p = p0 + tid + k * kNCT;
-        mv[k] = -INFINITY;
-        lv[k] = 0.f;
-        if (p < npieces * G) {
-          const int c = p / G, h = p - c * G;
-          const float* sl = a.ws_part + ((int64_t)(c0 + c + s) * G + h) * kSH;
-          mv[k] = ld_cg(sl + HD);
-          lv[k] = ld_cg(sl + HD + 1);
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int p = p0 + tid + k * kNCT;
-        if (p < npieces * G) {
-          const int c = p / G, h = p - c * G;
-          mb[c * kMaxGroup + h] = mv[k];
-          lb[c * kMaxGroup + h] = lv[k];
-        }
-      }
-    }
-    consumer_sync(kNCT);
-    for (int h = warp; h < G; h += NW) {  // one warp per head, lanes over pieces
-      float M = -INFINITY;
-      for (int c = lane; c < npieces; c += 32) M = fmaxf(M, mb[c * kMaxGroup + h]);
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-      float L = 0.f;
-      for (int c = lane; c < npieces; c += 32) {
-        const float w = (M == -INFINITY) ? 0.f : fast_exp2(mb[c * kMaxGroup + h] - M);
-        mb[c * kMaxGroup + h] = w;
-        L += w * lb[c * kMaxGroup + h];
-      }
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-      if (lane == 0) {
-        MLb[h] = M;
-        MLb[kMaxGroup + h] = L;
-      }
-    }
-    consumer_sync(kNCT);
     constexpr int kD4 = HD / 4;
     const int64_t step = (int64_t)G * kSH;
     for (int idx = tid; idx < G * kD4; idx += kNCT) {
       const int h = idx / kD4, d = (idx - h * kD4) * 4;
-      const float* base = a.ws_part + ((int64_t)(c0 + s) * G + h) * kSH + d;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int c = 0; c < npieces; c += 16) {  // 16 predicated loads in flight
+      const float* base = a.ws_part + ((int64_t)(c0 + s) * G + h) * kSH;
+      float M = -INFINITY, L = 0.f;
+      float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c = 0; c < npieces; c += 16) {
         float4 v[16];
-#pragma unroll
-        for (int u = 0; u < 16; ++u)
-          v[u] = (c + u < npieces) ? ld_cg4(base + (c + u) * step) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float mv[16], lv[16];
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
-          const float w = (c + u < npieces) ? mb[(c + u) * kMaxGroup + h] : 0.f;
-          acc.x += w * v[u].x; acc.y += w * v[u].y; acc.z += w * v[u].z; acc.w += w * v[u].w;
+          if (c + u < npieces) {
+            const float* sl = base + (c + u) * step;
+            v[u] = ld_cg4(sl + d);
+            mv[u] = ld_cg(sl + HD);
+            lv[u] = ld_cg(sl + HD + 1);
+          } else {
+            v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            mv[u] = -INFINITY;
+            lv[u] = 0.f;
+          }
         }
+        float mb = M;
+#pragma unroll
+        for (int u = 0; u < 16; ++u) mb = fmaxf(mb, mv[u]);
+        if (mb == -INFINITY) continue;  // only empty pieces so far
+        const float sc = (M == -INFINITY) ? 0.f : fast_exp2(M - mb);
+        O.x *= sc; O.y *= sc; O.z *= sc; O.w *= sc;
+        L *= sc;
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const float w = (mv[u] == -INFINITY) ? 0.f : fast_exp2(mv[u] - mb);
+          O.x += w * v[u].x; O.y += w * v[u].y; O.z += w * v[u].z; O.w += w * v[u].w;
+          L += w * lv[u];
+        }
+        M = mb;
       }
-      write_final4<HD>(a, b, g * G + h, d, acc, MLb[h], MLb[kMaxGroup + h]);
+      write_final4<HD>(a, b, g * G + h, d, O, M, L);
     }
   };
 
@@ -727,7 +802,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
     consumer_sync(kNCT);
     const int s = b * n_kv + g;
     int32_t c0;
-    const int32_t npieces = segment_pieces(sp, seq_start, ntiles, b, g, &c0);
+    const int32_t npieces = segment_pieces(sp, seq_start, nunits, b, g, &c0);
     for (int idx = tid; idx < G * HD; idx += kNCT) {
       const int h = idx / HD, d = idx - h * HD;
       float M = -INFINITY;
@@ -769,24 +844,31 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
     consumer_sync(kNCT);
   };
 
-  for (int32_t i = 0; i < my_count; ++i) {
-    if (tr.b != cur_b || tr.g != cur_g) {
-      if (cur_b >= 0) finish_piece(cur_b, cur_g);
-      cur_b = tr.b;
-      cur_g = tr.g;
-      load_q(cur_b, cur_g);
-      cons.begin(a, qs, lane);
+  // Piece by piece, tile by tile: the inner loop carries only the ring
+  // position and the row cursor, so the consumer keeps its registers.
+  TileWalk wk;
+  wk.init(seq_start, nunits, B, my_lo, my_lo + my_count);
+  Piece pc;
+  int st = 0;
+  uint32_t phase = 0;
+  while (wk.next_piece(nunits, B, n_kv, pc)) {
+    load_q(pc.b, pc.g);
+    cons.begin(a, qs, lane);
+    const int np = npos[pc.b];
+    int row0 = pc.u0 * unit_rows;
+    for (int k = 0; k < pc.n; ++k, row0 += unit_rows) {
+      const int rows = imin(unit_rows, np - row0);
+      mbar_wait(&full[st], phase, flags, a.status);
+      cons.consume(a, smem + (size_t)st * a.stage_bytes, rows, pbuf_w, qs, warp, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+      if (++st == a.stages) {
+        st = 0;
+        phase ^= 1u;
+      }
     }
-    const int st = i % a.stages;
-    const uint32_t use = (uint32_t)(i / a.stages);
-    const int rows = min(a.tile, npos[tr.b] - tr.j * a.tile);
-    mbar_wait(&full[st], use & 1u, flags, a.status);
-    cons.consume(a, smem + (size_t)st * a.stage_bytes, rows, pbuf_w, qs, warp, lane);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
-    next_tile(tr, ntiles, B, n_kv);
+    finish_piece(pc.b, pc.g);
   }
-  finish_piece(cur_b, cur_g);
 }
 
 }  // namespace gla

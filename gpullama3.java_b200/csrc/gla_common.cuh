@@ -27,14 +27,16 @@ constexpr int kMaxBatch = 1024;
 // ---------------------------------------------------------------------------
 // Split-KV work partition.
 //
-// The decode work of a call is the list of tiles ordered by
-// (sequence b, kv head g, tile j): segment s = b*n_kv + g holds
-// ntiles(b) = ceil(n_pos[b]/tile) tiles.  The W tiles are dealt to P CTAs in
-// contiguous, near-equal ranges (the first W%P CTAs get one extra), so every
-// CTA streams the same number of KV bytes (+-1 tile) whatever the sequence
-// lengths.  The intersection of a CTA range with a segment is a "piece"; the
-// piece of (CTA c, segment s) owns partial slot c + s, which is unique because
-// walking the tile list each new piece increments c, s, or both.
+// The decode work of a call is the list of units of `unit_rows` rows (the
+// decode kernels use whole tiles) ordered by (sequence b, kv head g, unit u):
+// segment s = b*n_kv + g holds nunits(b) = ceil(n_pos[b]/unit_rows) units.
+// The W units are dealt to P CTAs in contiguous, near-equal ranges (the first
+// W%P CTAs get one extra unit), so every CTA streams the same number of KV
+// bytes (+- one unit) whatever the sequence lengths.  A CTA walks its range
+// in tiles of up to `tile_units` units that never cross a segment boundary.  The intersection of a CTA
+// range with a segment is a "piece"; the piece of (CTA c, segment s) owns
+// partial slot c + s, which is unique because walking the unit list each new
+// piece increments c, s, or both.
 // ---------------------------------------------------------------------------
 struct Split {
   int32_t q;  // W / P
@@ -47,7 +49,7 @@ GLA_HD int32_t split_lo(Split sp, int32_t c) { return c * sp.q + (c < sp.r ? c :
 
 GLA_HD int32_t split_count(Split sp, int32_t c) { return sp.q + (c < sp.r ? 1 : 0); }
 
-// CTA that owns tile t.
+// CTA that owns unit t.
 GLA_HD int32_t split_owner(Split sp, int32_t t) {
   int32_t big = sp.r * (sp.q + 1);
   if (t < big) return t / (sp.q + 1);
@@ -55,53 +57,95 @@ GLA_HD int32_t split_owner(Split sp, int32_t t) {
 }
 
 GLA_HD int32_t ceil_div(int32_t a, int32_t b) { return (a + b - 1) / b; }
+GLA_HD int32_t imin(int32_t a, int32_t b) { return a < b ? a : b; }
 
-// Position of a tile inside the work list.
-struct TileRef {
-  int32_t b;    // sequence
-  int32_t g;    // kv head
-  int32_t j;    // tile index inside the segment
-  int32_t nt;   // tiles of this sequence's segments
+// One tile of a CTA's walk.
+struct Tile {
+  int32_t b;      // sequence
+  int32_t g;      // kv head
+  int32_t row0;   // first row inside the segment
+  int32_t units;  // 16-row units (rows may end earlier at the segment's last row)
 };
 
-// Locates global tile t given the per-sequence tile prefix
-// seq_start[b] = n_kv * sum_{b'<b} ntiles(b') (length n_seq + 1).
-GLA_HD TileRef locate_tile(const int32_t* seq_start, const int32_t* ntiles, int32_t n_seq,
-                           int32_t n_kv, int32_t t) {
-  int32_t lo = 0, hi = n_seq - 1;
-  while (lo < hi) {  // last b with seq_start[b] <= t (sequences with 0 tiles are skipped)
-    int32_t mid = (lo + hi + 1) >> 1;
-    if (seq_start[mid] <= t) lo = mid; else hi = mid - 1;
+// The units [u0, u0 + n) of segment (b, g) that one CTA holds.
+struct Piece {
+  int32_t b, g, u0, n;
+};
+
+// Walker over a CTA's unit range [p, end) given the per-sequence unit prefix
+// seq_start[b] = n_kv * sum_{b'<b} nunits(b') (length n_seq + 1).
+struct TileWalk {
+  int32_t p, end;
+  int32_t b, g, nu;
+  int32_t seg_lo, seg_hi;
+
+  GLA_HD void init(const int32_t* seq_start, const int32_t* nunits, int32_t n_seq, int32_t lo,
+                   int32_t hi) {
+    p = lo;
+    end = hi;
+    b = g = nu = seg_lo = seg_hi = 0;
+    if (lo >= hi) return;
+    int32_t l = 0, h = n_seq - 1;
+    while (l < h) {  // last b with seq_start[b] <= lo (sequences with no units are skipped)
+      const int32_t mid = (l + h + 1) >> 1;
+      if (seq_start[mid] <= lo) l = mid; else h = mid - 1;
+    }
+    while (l < n_seq - 1 && seq_start[l + 1] <= lo) ++l;
+    b = l;
+    nu = nunits[b];
+    g = (lo - seq_start[b]) / nu;
+    seg_lo = seq_start[b] + g * nu;
+    seg_hi = seg_lo + nu;
   }
-  while (lo < n_seq - 1 && seq_start[lo + 1] <= t) ++lo;
-  TileRef r;
-  r.b = lo;
-  r.nt = ntiles[lo];
-  int32_t off = t - seq_start[lo];
-  r.g = off / r.nt;
-  r.j = off - r.g * r.nt;
-  (void)n_kv;
-  return r;
-}
 
-// Advances a TileRef to the next tile of the work list.
-GLA_HD void next_tile(TileRef& r, const int32_t* ntiles, int32_t n_seq, int32_t n_kv) {
-  if (++r.j < r.nt) return;
-  r.j = 0;
-  if (++r.g < n_kv) return;
-  r.g = 0;
-  do {
-    ++r.b;
-  } while (r.b < n_seq && ntiles[r.b] == 0);
-  if (r.b < n_seq) r.nt = ntiles[r.b];
-}
+  // Next tile of at most tile_units units of unit_rows rows; false when the
+  // range is done.
+  GLA_HD bool next(const int32_t* nunits, int32_t n_seq, int32_t n_kv, int32_t tile_units,
+                   int32_t unit_rows, Tile& t) {
+    if (p >= end) return false;
+    const int32_t n = imin(tile_units, imin(seg_hi - p, end - p));
+    t.b = b;
+    t.g = g;
+    t.row0 = (p - seg_lo) * unit_rows;
+    t.units = n;
+    advance(nunits, n_seq, n_kv, n);
+    return true;
+  }
 
-// Number of CTAs holding a piece of segment (b, g).
-GLA_HD int32_t segment_pieces(Split sp, const int32_t* seq_start, const int32_t* ntiles,
-                              int32_t b, int32_t g, int32_t* first_cta) {
-  int32_t t0 = seq_start[b] + g * ntiles[b];
-  int32_t t1 = t0 + ntiles[b] - 1;
-  int32_t c0 = split_owner(sp, t0);
+  // Next piece: the rest of the range inside the current segment.
+  GLA_HD bool next_piece(const int32_t* nunits, int32_t n_seq, int32_t n_kv, Piece& pc) {
+    if (p >= end) return false;
+    const int32_t n = imin(seg_hi - p, end - p);
+    pc.b = b;
+    pc.g = g;
+    pc.u0 = p - seg_lo;
+    pc.n = n;
+    advance(nunits, n_seq, n_kv, n);
+    return true;
+  }
+
+  GLA_HD void advance(const int32_t* nunits, int32_t n_seq, int32_t n_kv, int32_t n) {
+    p += n;
+    if (p == seg_hi && p < end) {  // step to the next segment
+      if (++g == n_kv) {
+        g = 0;
+        do {
+          ++b;
+        } while (b < n_seq && nunits[b] == 0);
+        nu = b < n_seq ? nunits[b] : 1;
+      }
+      seg_lo = p;
+      seg_hi = p + nu;
+    }
+  }
+};
+
+// Number of CTAs holding a piece of segment (b, g); *first_cta the first.
+GLA_HD int32_t segment_pieces(Split sp, const int32_t* seq_start, const int32_t* nunits, int32_t b,
+                              int32_t g, int32_t* first_cta) {
+  const int32_t t0 = seq_start[b] + g * nunits[b];
+  const int32_t t1 = t0 + nunits[b] - 1;
+  const int32_t c0 = split_owner(sp, t0);
   *first_cta = c0;
   return split_owner(sp, t1) - c0 + 1;
 }
@@ -257,6 +301,38 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 }
 
 __device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
+
+// ---- packed FP32 pairs (sm_100 f32x2 instructions) -----------------------
+// A pair is a b64 register: element 0 in the low half, element 1 in the high
+// half, the same order as two consecutive floats in memory.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 
 #endif  // __CUDACC__
 

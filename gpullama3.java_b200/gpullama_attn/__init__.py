@@ -24,6 +24,7 @@ DTYPE_F32 = 0
 DTYPE_F16 = 1
 ROPE_INTERLEAVED = 0
 ROPE_NEOX = 1
+OPT_EARLY_KV_PREFETCH = 1
 
 STATUS_NAMES = {
     0: "GLA_OK", -1: "GLA_ERR_INVALID_ARG", -2: "GLA_ERR_CUDA", -3: "GLA_ERR_NOT_SUPPORTED",
@@ -47,6 +48,7 @@ _SIGS = {
     "gla_device_status": (_I32, [_P, ctypes.POINTER(_I32)]),
     "gla_reserve": (_I32, [_P, _I32, _I32, _I32, _I32]),
     "gla_num_sms": (_I32, [_P]),
+    "gla_set_option": (_I32, [_P, _I32, _I32]),
     "gla_kv_cache_alloc": (_I32, [_P, _I32, _I32, _I32, _I32, ctypes.POINTER(_P),
                                   ctypes.POINTER(_P)]),
     "gla_kv_cache_free": (_I32, [_P, _P, _P]),
@@ -70,7 +72,8 @@ _SIGS = {
     "gla_decode_sharded_f32kv": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F]),
     "gla_prefill_causal_f16": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _F]),
     "gla_rope_append_f32": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P, _F, _I32]),
-    "gla_debug_partition": (_I64, [_P, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _I64]),
+    "gla_debug_partition": (_I64, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P,
+                                   _I64]),
     "gla_decode_f32kv_noalloc": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F, _P]),
 }
 
@@ -114,19 +117,19 @@ def _ptr(x) -> int | None:
     raise TypeError(f"expected a device tensor or an address, got {type(x)!r}")
 
 
-def debug_partition(n_pos, n_kv_heads, tile, n_ctas):
-    """Host run of the decode work partition (no GPU). Returns a dict of lists."""
+def debug_partition(n_pos, n_kv_heads, tile, n_ctas, unit_rows=16):
+    """Host run of the decode work partition (no GPU). Returns a dict of arrays."""
     import numpy as np
 
     n_pos = np.ascontiguousarray(n_pos, dtype=np.int32)
-    total = int(sum((max(int(x), 0) + tile - 1) // tile for x in n_pos)) * n_kv_heads
-    cap = max(total, 1)
-    arrs = [np.zeros(cap, dtype=np.int32) for _ in range(5)]
-    rc = lib().gla_debug_partition(n_pos.ctypes.data, len(n_pos), n_kv_heads, tile, n_ctas,
-                                   *[a.ctypes.data for a in arrs], cap)
+    units = int(sum((max(int(x), 0) + unit_rows - 1) // unit_rows for x in n_pos)) * n_kv_heads
+    cap = max(units + n_ctas + len(n_pos) * n_kv_heads, 1)
+    arrs = [np.zeros(cap, dtype=np.int32) for _ in range(6)]
+    rc = lib().gla_debug_partition(n_pos.ctypes.data, len(n_pos), n_kv_heads, tile, unit_rows,
+                                   n_ctas, *[a.ctypes.data for a in arrs], cap)
     if rc < 0:
         raise GlaError(int(rc), "gla_debug_partition")
-    names = ("cta", "seq", "kv_head", "row0", "slot")
+    names = ("cta", "seq", "kv_head", "row0", "rows", "slot")
     return {k: a[:rc] for k, a in zip(names, arrs)}
 
 
@@ -181,6 +184,9 @@ class Context:
 
     def num_sms(self) -> int:
         return int(self._L.gla_num_sms(self._h))
+
+    def set_option(self, option: int, value: int):
+        self._check(self._L.gla_set_option(self._h, option, value), "gla_set_option")
 
     def device_status(self) -> int:
         st = _I32(0)

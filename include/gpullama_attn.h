@@ -91,6 +91,18 @@ int32_t gla_reserve(gla_ctx* ctx, int32_t max_batch, int32_t max_kv_heads, int32
 /* Number of streaming multiprocessors of the context's device. */
 int32_t gla_num_sms(const gla_ctx* ctx);
 
+/* Context options (gla_set_option). */
+#define GLA_OPT_EARLY_KV_PREFETCH 1
+/* GLA_OPT_EARLY_KV_PREFETCH (default 1): decode calls that take n_pos from
+ * the host (gla_decode_*, gla_decode_partial_*, gla_decode_sharded_*) launch
+ * with programmatic dependent launch and may start reading K/V rows
+ * [0, n_pos - 1) - the cache history - before the kernel issued just before
+ * them on the stream has finished.  The newest row (n_pos - 1), q and every
+ * other input are read only after it has finished.  Set 0 if a kernel that
+ * runs right before a decode call, and releases its dependents early
+ * (griddepcontrol.launch_dependents), writes older cache rows. */
+int32_t gla_set_option(gla_ctx* ctx, int32_t option, int32_t value);
+
 /* ------------------------------------------------------------------------ */
 /* KV cache allocation (device MemorySegments of State)                      */
 /* ------------------------------------------------------------------------ */
@@ -287,13 +299,16 @@ int32_t gla_rope_append_f32(gla_ctx* ctx, float* q, float* k, const float* v, fl
 /* ------------------------------------------------------------------------ */
 
 /* Runs the decode kernels' work partition on the host: `n_seq` sequences with
- * n_pos[] rows, n_kv_heads segments each, tiles of `tile` rows over `n_ctas`
- * CTAs.  Writes for every tile (in work order) its CTA, sequence, kv head,
- * first row and partial-slot index into the five arrays (each of length
+ * n_pos[] rows, n_kv_heads segments each, dealt to `n_ctas` CTAs in units of
+ * `unit_rows` rows and walked in tiles of up to `tile` rows (a multiple of
+ * unit_rows).  Writes
+ * for every tile, in walk order, its CTA, sequence, kv head, first row, row
+ * count and partial-slot index into the six arrays (each of length
  * `capacity`); returns the tile count or a negative status. */
 int64_t gla_debug_partition(const int32_t* n_pos, int32_t n_seq, int32_t n_kv_heads, int32_t tile,
-                            int32_t n_ctas, int32_t* cta, int32_t* seq, int32_t* kv_head,
-                            int32_t* row0, int32_t* slot, int64_t capacity);
+                            int32_t unit_rows, int32_t n_ctas, int32_t* cta, int32_t* seq,
+                            int32_t* kv_head, int32_t* row0, int32_t* rows, int32_t* slot,
+                            int64_t capacity);
 
 #ifdef __cplusplus
 }

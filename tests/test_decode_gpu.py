@@ -289,3 +289,40 @@ def test_rope_append_matches_oracle(gla_ctx, oracle):
         np.testing.assert_array_equal(kc[pos].cpu().numpy(), kd.cpu().numpy())
         np.testing.assert_array_equal(vc[pos].cpu().numpy(), vin)
         assert float(kc[:pos].abs().sum()) == 0.0
+
+
+def test_early_prefetch_sees_the_row_appended_just_before(gla_ctx, oracle):
+    """RoPE + KV append writes row `pos`, then a decode over rows 0..pos runs
+    right after it on the same stream: the early history prefetch must not
+    read the newest row before the append has finished, and the result must
+    not depend on the option."""
+    import gpullama_attn as gla
+
+    torch = _torch()
+    nh, nkv, hd, T = 24, 8, 128, 2000
+    pos = T - 1
+    q0, k, v = inputs.decode_case(51, nh, nkv, hd, T)
+    rng = np.random.Generator(np.random.PCG64(52))
+    knew = rng.standard_normal(nkv * hd, dtype=np.float32)
+    vnew = rng.standard_normal(nkv * hd, dtype=np.float32)
+    k[pos] = 7.0  # stale row contents the append must replace
+    v[pos] = -7.0
+    outs = []
+    for opt in (1, 0):
+        gla_ctx.set_option(gla.OPT_EARLY_KV_PREFETCH, opt)
+        kc, vc = dev(k), dev(v)
+        qd, kd, vd = dev(q0), dev(knew), dev(vnew)
+        ph = torch.tensor([pos], dtype=torch.int32, device="cuda")
+        xb = torch.empty(nh * hd, device="cuda")
+        for _ in range(3):  # back-to-back decodes: PDL overlap between them
+            gla_ctx.decode(qd, kc, vc, xb, nh, nkv, hd, pos)
+        gla_ctx.rope_append(qd, kd, vd, kc, vc, nh, nkv, hd, ph, 500000.0)
+        gla_ctx.decode(qd, kc, vc, xb, nh, nkv, hd, pos + 1)
+        assert gla_ctx.device_status() == 0
+        outs.append(xb.cpu().numpy())
+        kk, vv, qq = kc.cpu().numpy(), vc.cpu().numpy(), qd.cpu().numpy()
+        ref = oracle.decode_f32(qq, kk, vv, nh, nkv, hd, pos + 1)
+        assert_close(outs[-1], ref, TOL_F32, f"option {opt}")
+        assert np.abs(kk[pos]).max() < 7.0 and vv[pos][0] == vnew[0]
+    gla_ctx.set_option(gla.OPT_EARLY_KV_PREFETCH, 1)
+    np.testing.assert_array_equal(outs[0], outs[1])
