@@ -584,7 +584,7 @@ int32_t gla_rope_append_f32(gla_ctx* ctx, float* q, float* k, const float* v, fl
 int64_t gla_debug_partition(const int32_t* n_pos, int32_t n_seq, int32_t n_kv_heads, int32_t tile,
                             int32_t unit_rows, int32_t n_ctas, int32_t* cta, int32_t* seq,
                             int32_t* kv_head, int32_t* row0, int32_t* rows, int32_t* slot,
-                            int64_t capacity) {
+                            int32_t* first_cta, int32_t* npieces, int64_t capacity) {
   if (!n_pos || n_seq < 1 || n_kv_heads < 1 || n_ctas < 1 || unit_rows < 1 || tile < unit_rows ||
       tile % unit_rows != 0)
     return GLA_ERR_INVALID_ARG;
@@ -597,11 +597,12 @@ int64_t gla_debug_partition(const int32_t* n_pos, int32_t n_seq, int32_t n_kv_he
     acc += nunits[b];
   }
   start[n_seq] = (int32_t)(acc * n_kv_heads);
-  const gla::Split sp = gla::make_split(start[n_seq], n_ctas);
+  const gla::Deal deal = gla::make_deal(start[n_seq], n_ctas, n_seq, n_kv_heads, nunits[0]);
   // walk each CTA's range exactly as the kernel's producer and consumers do
   int64_t n = 0;
   for (int32_t c = 0; c < n_ctas; ++c) {
-    const int32_t lo = gla::split_lo(sp, c), cnt = gla::split_count(sp, c);
+    int32_t lo, cnt;
+    deal.range(c, &lo, &cnt);
     gla::TileWalk wk;
     wk.init(start.data(), nunits.data(), n_seq, lo, lo + cnt);
     gla::Tile t;
@@ -613,6 +614,10 @@ int64_t gla_debug_partition(const int32_t* n_pos, int32_t n_seq, int32_t n_kv_he
       row0[n] = t.row0;
       rows[n] = std::min(t.units * unit_rows, np[t.b] - t.row0);
       slot[n] = c + t.b * n_kv_heads + t.g;
+      int32_t c0;
+      const int32_t np_ = deal.pieces(start.data(), nunits.data(), t.b, t.g, &c0);
+      first_cta[n] = c0;
+      npieces[n] = np_;
       ++n;
     }
   }

@@ -525,7 +525,6 @@ __device__ __forceinline__ void write_final(const DecodeArgs& a, int b, int hq, 
 template <int HD>
 __device__ __forceinline__ void write_final4(const DecodeArgs& a, int b, int hq, int d, float4 O,
                                              float M, float L) {
-  const float inv = L > 0.f ? 1.f / L : 0.f;
   if (a.record_mode) {
     write_final<HD>(a, b, hq, d, O.x, M, L);
     write_final<HD>(a, b, hq, d + 1, O.y, M, L);
@@ -538,7 +537,6 @@ __device__ __forceinline__ void write_final4(const DecodeArgs& a, int b, int hq,
     r.y = L > 0.f ? O.y / L : 0.f;
     r.z = L > 0.f ? O.z / L : 0.f;
     r.w = L > 0.f ? O.w / L : 0.f;
-    (void)inv;
     *reinterpret_cast<float4*>(a.out + row * HD + d) = r;
   }
 }
@@ -638,24 +636,26 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   // kernels (the only kernels here that release dependents early) never write
   // a cache; a preceding kernel that does not release dependents has finished
   // before this grid starts.
+  // The ring's first pass (up to `stages` tiles) is walked here; a tile
+  // holding a sequence's newest row is skipped (bit k of `late`) and fetched
+  // after the wait, the tiles behind it are not held back.
   const bool early = LOADER == 0 && a.early_kv && a.n_pos_dev == nullptr;
   int32_t n_early = 0;
+  uint32_t late = 0;
   if (early) {
     scan_sequences();
     __syncthreads();
     if (warp == NW && lane == 0) {
-      const Split sp0 = make_split(seq_start[B], (int32_t)gridDim.x);
-      const int32_t lo = split_lo(sp0, blockIdx.x), cnt = split_count(sp0, blockIdx.x);
+      const Deal d0 = make_deal(seq_start[B], (int32_t)gridDim.x, B, n_kv, nunits[0]);
+      int32_t lo, cnt;
+      d0.range(blockIdx.x, &lo, &cnt);
       const uint64_t pol = l2_evict_first_policy();
       TileWalk wk;
       wk.init(seq_start, nunits, B, lo, lo + cnt);
       Tile t;
-      while (n_early < a.stages) {
-        TileWalk probe = wk;
-        if (!probe.next(nunits, B, n_kv, tile_units, unit_rows, t)) break;
-        if (t.row0 + t.units * unit_rows >= npos[t.b]) break;  // holds the newest row
-        wk = probe;
-        tma_tile(n_early, t, pol);
+      while (n_early < a.stages && wk.next(nunits, B, n_kv, tile_units, unit_rows, t)) {
+        if (t.row0 + t.units * unit_rows >= npos[t.b]) late |= 1u << n_early;  // newest row
+        else tma_tile(n_early, t, pol);
         ++n_early;
       }
     }
@@ -668,19 +668,24 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   __syncthreads();
 
   const int32_t W = seq_start[B];
-  const Split sp = make_split(W, (int32_t)gridDim.x);
-  const int32_t my_lo = split_lo(sp, blockIdx.x);
-  const int32_t my_count = split_count(sp, blockIdx.x);
+  const Deal deal = make_deal(W, (int32_t)gridDim.x, B, n_kv, nunits[0]);
+  int32_t my_lo, my_count;
+  deal.range(blockIdx.x, &my_lo, &my_count);
 
   if (warp == NW) {
     // ---------------- producer ----------------
     if (my_count > 0) {
       const uint64_t pol = l2_evict_first_policy();
       const int32_t first = early ? __shfl_sync(0xffffffffu, n_early, 0) : 0;
+      const uint32_t late_mask = early ? __shfl_sync(0xffffffffu, late, 0) : 0u;
       TileWalk wk;
       wk.init(seq_start, nunits, B, my_lo, my_lo + my_count);
       Tile t;
-      for (int32_t k = 0; k < first; ++k) wk.next(nunits, B, n_kv, tile_units, unit_rows, t);
+      for (int32_t k = 0; k < first; ++k) {  // first ring pass: no empty-barrier waits
+        wk.next(nunits, B, n_kv, tile_units, unit_rows, t);
+        if (lane == 0 && ((late_mask >> k) & 1u)) tma_tile(k, t, pol);
+      }
+      __syncwarp();
       int cur_b = -1;
       const char* kb = nullptr;
       const char* vb = nullptr;
@@ -751,49 +756,71 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   };
 
   // Merges the pieces of segment (b, g) held in workspace slots c + s for
-  // c in [c0, c0 + npieces).  Each thread owns (head, 4 columns) elements and
-  // folds the pieces in with a running log-sum-exp, 16 pieces per round of
-  // loads: no shared memory and no barrier.
+  // c in [c0, c0 + npieces).  An item is (head, 4 columns); tpi adjacent
+  // threads share an item (as many as fill the consumer threads), each
+  // folding every tpi-th piece in with a running log-sum-exp, 16 pieces per
+  // round of loads (one round up to 16 * tpi pieces); shuffles then join the
+  // tpi partial results.  No shared memory and no barrier.
   auto combine_pieces = [&](int b, int g, int s, int c0, int npieces) {
     constexpr int kD4 = HD / 4;
+    const int items = G * kD4;
+    int tpi = 1;
+    while (tpi < 8 && items * tpi * 2 <= kNCT) tpi *= 2;
     const int64_t step = (int64_t)G * kSH;
-    for (int idx = tid; idx < G * kD4; idx += kNCT) {
-      const int h = idx / kD4, d = (idx - h * kD4) * 4;
-      const float* base = a.ws_part + ((int64_t)(c0 + s) * G + h) * kSH;
+    for (int base = 0; base < items * tpi; base += kNCT) {  // warp-uniform trip count
+      const int idx = base + tid;
+      const bool active = idx < items * tpi;
+      const int it = active ? idx / tpi : 0, j = idx % tpi;
+      const int h = it / kD4, d = (it - h * kD4) * 4;
+      const float* sbase = a.ws_part + ((int64_t)(c0 + s) * G + h) * kSH;
       float M = -INFINITY, L = 0.f;
       float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int c = 0; c < npieces; c += 16) {
+      for (int c = active ? j : npieces; c < npieces; c += 16 * tpi) {
         float4 v[16];
-        float mv[16], lv[16];
+        float2 ml[16];
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
-          if (c + u < npieces) {
-            const float* sl = base + (c + u) * step;
+          if (c + u * tpi < npieces) {
+            const float* sl = sbase + (c + u * tpi) * step;
             v[u] = ld_cg4(sl + d);
-            mv[u] = ld_cg(sl + HD);
-            lv[u] = ld_cg(sl + HD + 1);
+            ml[u] = ld_cg2(sl + HD);
           } else {
             v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-            mv[u] = -INFINITY;
-            lv[u] = 0.f;
+            ml[u] = make_float2(-INFINITY, 0.f);
           }
         }
         float mb = M;
 #pragma unroll
-        for (int u = 0; u < 16; ++u) mb = fmaxf(mb, mv[u]);
+        for (int u = 0; u < 16; ++u) mb = fmaxf(mb, ml[u].x);
         if (mb == -INFINITY) continue;  // only empty pieces so far
         const float sc = (M == -INFINITY) ? 0.f : fast_exp2(M - mb);
         O.x *= sc; O.y *= sc; O.z *= sc; O.w *= sc;
         L *= sc;
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
-          const float w = (mv[u] == -INFINITY) ? 0.f : fast_exp2(mv[u] - mb);
+          const float w = (ml[u].x == -INFINITY) ? 0.f : fast_exp2(ml[u].x - mb);
           O.x += w * v[u].x; O.y += w * v[u].y; O.z += w * v[u].z; O.w += w * v[u].w;
-          L += w * lv[u];
+          L += w * ml[u].y;
         }
         M = mb;
       }
-      write_final4<HD>(a, b, g * G + h, d, O, M, L);
+      for (int off = 1; off < tpi; off <<= 1) {
+        const float Mo = __shfl_xor_sync(0xffffffffu, M, off);
+        const float Lo = __shfl_xor_sync(0xffffffffu, L, off);
+        float4 Oo;
+        Oo.x = __shfl_xor_sync(0xffffffffu, O.x, off);
+        Oo.y = __shfl_xor_sync(0xffffffffu, O.y, off);
+        Oo.z = __shfl_xor_sync(0xffffffffu, O.z, off);
+        Oo.w = __shfl_xor_sync(0xffffffffu, O.w, off);
+        const float Mn = fmaxf(M, Mo);
+        const float sa = (M == -INFINITY) ? 0.f : fast_exp2(M - Mn);
+        const float sb = (Mo == -INFINITY) ? 0.f : fast_exp2(Mo - Mn);
+        O.x = O.x * sa + Oo.x * sb; O.y = O.y * sa + Oo.y * sb;
+        O.z = O.z * sa + Oo.z * sb; O.w = O.w * sa + Oo.w * sb;
+        L = L * sa + Lo * sb;
+        M = Mn;
+      }
+      if (active && j == 0) write_final4<HD>(a, b, g * G + h, d, O, M, L);
     }
   };
 
@@ -802,7 +829,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
     consumer_sync(kNCT);
     const int s = b * n_kv + g;
     int32_t c0;
-    const int32_t npieces = segment_pieces(sp, seq_start, nunits, b, g, &c0);
+    const int32_t npieces = deal.pieces(seq_start, nunits, b, g, &c0);
     for (int idx = tid; idx < G * HD; idx += kNCT) {
       const int h = idx / HD, d = idx - h * HD;
       float M = -INFINITY;

@@ -150,6 +150,59 @@ GLA_HD int32_t segment_pieces(Split sp, const int32_t* seq_start, const int32_t*
   return split_owner(sp, t1) - c0 + 1;
 }
 
+// How the W units of a call are dealt to P CTAs.
+//  contiguous (mode 0): Split(W, P) over the (b, g, u) order; a CTA range may
+//    straddle segments and then holds several pieces.
+//  per segment (mode 1; one sequence, n_kv <= P): kv head g gets the CTAs of
+//    group g of Split(P, n_kv), which split its nu units evenly, so no CTA
+//    holds more than one piece -- a piece boundary inside a CTA's range
+//    stalls its consumers for a partial write and counter round trip, and a
+//    late CTA becomes its segment's merger.  The largest CTA share is the
+//    same as the contiguous deal's when n_kv divides P, within one unit
+//    otherwise.
+// Either way the pieces of a segment are consecutive CTAs, and piece
+// (CTA c, segment s) owns partial slot c + s.
+struct Deal {
+  int32_t mode;
+  Split sp;    // mode 0: Split(W, P); mode 1: Split(P, n_kv)
+  int32_t nu;  // mode 1: units per segment
+
+  GLA_HD void range(int32_t c, int32_t* lo, int32_t* cnt) const {
+    if (mode == 0) {
+      *lo = split_lo(sp, c);
+      *cnt = split_count(sp, c);
+      return;
+    }
+    const int32_t g = split_owner(sp, c);
+    const Split su = make_split(nu, split_count(sp, g));
+    const int32_t j = c - split_lo(sp, g);
+    *lo = g * nu + split_lo(su, j);
+    *cnt = split_count(su, j);
+  }
+
+  GLA_HD int32_t pieces(const int32_t* seq_start, const int32_t* nunits, int32_t b, int32_t g,
+                        int32_t* first_cta) const {
+    if (mode == 0) return segment_pieces(sp, seq_start, nunits, b, g, first_cta);
+    *first_cta = split_lo(sp, g);
+    return imin(split_count(sp, g), nu);
+  }
+};
+
+// W = total units, P = CTAs, nu0 = units of sequence 0.
+GLA_HD Deal make_deal(int32_t W, int32_t P, int32_t n_seq, int32_t n_kv, int32_t nu0) {
+  Deal d;
+  if (n_seq == 1 && n_kv <= P && nu0 > 0) {
+    d.mode = 1;
+    d.sp = make_split(P, n_kv);
+    d.nu = nu0;
+  } else {
+    d.mode = 0;
+    d.sp = make_split(W, P);
+    d.nu = 0;
+  }
+  return d;
+}
+
 #ifdef __CUDACC__
 
 // ---------------------------------------------------------------------------
@@ -279,6 +332,10 @@ __device__ __forceinline__ void consumer_sync(int nthreads) {
 }
 
 __device__ __forceinline__ float ld_cg(const float* p) { return __ldcg(p); }
+
+__device__ __forceinline__ float2 ld_cg2(const float* p) {
+  return __ldcg(reinterpret_cast<const float2*>(p));
+}
 
 __device__ __forceinline__ float4 ld_cg4(const float* p) {
   return __ldcg(reinterpret_cast<const float4*>(p));

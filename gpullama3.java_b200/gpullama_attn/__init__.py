@@ -73,7 +73,7 @@ _SIGS = {
     "gla_prefill_causal_f16": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _F]),
     "gla_rope_append_f32": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P, _F, _I32]),
     "gla_debug_partition": (_I64, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P,
-                                   _I64]),
+                                   _P, _P, _I64]),
     "gla_decode_f32kv_noalloc": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F, _P]),
 }
 
@@ -117,19 +117,19 @@ def _ptr(x) -> int | None:
     raise TypeError(f"expected a device tensor or an address, got {type(x)!r}")
 
 
-def debug_partition(n_pos, n_kv_heads, tile, n_ctas, unit_rows=16):
+def debug_partition(n_pos, n_kv_heads, tile, n_ctas, unit_rows=64):
     """Host run of the decode work partition (no GPU). Returns a dict of arrays."""
     import numpy as np
 
     n_pos = np.ascontiguousarray(n_pos, dtype=np.int32)
     units = int(sum((max(int(x), 0) + unit_rows - 1) // unit_rows for x in n_pos)) * n_kv_heads
     cap = max(units + n_ctas + len(n_pos) * n_kv_heads, 1)
-    arrs = [np.zeros(cap, dtype=np.int32) for _ in range(6)]
+    arrs = [np.zeros(cap, dtype=np.int32) for _ in range(8)]
     rc = lib().gla_debug_partition(n_pos.ctypes.data, len(n_pos), n_kv_heads, tile, unit_rows,
                                    n_ctas, *[a.ctypes.data for a in arrs], cap)
     if rc < 0:
         raise GlaError(int(rc), "gla_debug_partition")
-    names = ("cta", "seq", "kv_head", "row0", "rows", "slot")
+    names = ("cta", "seq", "kv_head", "row0", "rows", "slot", "first_cta", "npieces")
     return {k: a[:rc] for k, a in zip(names, arrs)}
 
 

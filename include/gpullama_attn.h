@@ -301,14 +301,15 @@ int32_t gla_rope_append_f32(gla_ctx* ctx, float* q, float* k, const float* v, fl
 /* Runs the decode kernels' work partition on the host: `n_seq` sequences with
  * n_pos[] rows, n_kv_heads segments each, dealt to `n_ctas` CTAs in units of
  * `unit_rows` rows and walked in tiles of up to `tile` rows (a multiple of
- * unit_rows).  Writes
- * for every tile, in walk order, its CTA, sequence, kv head, first row, row
- * count and partial-slot index into the six arrays (each of length
- * `capacity`); returns the tile count or a negative status. */
+ * unit_rows).  Writes for every tile, in walk order, its CTA, sequence, kv
+ * head, first row, row count, partial-slot index, and the first CTA and
+ * number of CTAs holding a piece of its segment (the merge's view) into the
+ * eight arrays (each of length `capacity`); returns the tile count or a
+ * negative status. */
 int64_t gla_debug_partition(const int32_t* n_pos, int32_t n_seq, int32_t n_kv_heads, int32_t tile,
                             int32_t unit_rows, int32_t n_ctas, int32_t* cta, int32_t* seq,
                             int32_t* kv_head, int32_t* row0, int32_t* rows, int32_t* slot,
-                            int64_t capacity);
+                            int32_t* first_cta, int32_t* npieces, int64_t capacity);
 
 #ifdef __cplusplus
 }
