@@ -53,7 +53,7 @@ Layout layout_for(int dtype, int hd, int group, int tile, int stages, int batch,
   off = L.off_pbuf +
         (dtype == GLA_DTYPE_F16 ? 0 : (size_t)nw * F32Consumer<128, 1>::kPbufFloats * sizeof(float));
   L.off_merge = (int32_t)align16(off);
-  off = L.off_merge + (size_t)nw * group_cap_for(dtype, group) * (hd + 2) * sizeof(float);
+  off = L.off_merge + (size_t)nw * group_cap_for(dtype, group) * (hd + 4) * sizeof(float);
   L.off_flags = (int32_t)align16(off);
   (void)grid;
   L.total = L.off_flags + 16 + 1024;  // + slack to 1024-align the stage ring

@@ -81,6 +81,9 @@ struct DecodeArgs {
 // Floats per head in a workspace piece slot: o[HD], m, l, 2 pad (16-byte rows).
 template <int HD>
 constexpr int slot_head_floats() { return HD + 4; }
+// Floats per head in a warp's merge buffer: the same 16-byte-row layout.
+template <int HD>
+constexpr int merge_head_floats() { return HD + 4; }
 
 constexpr float kLn2 = 0.69314718055994530942f;
 
@@ -276,7 +279,8 @@ struct F32Consumer {
     __syncwarp();
   }
 
-  // Writes this warp's (o, m, l) for q heads h < group into merge_w[h][HD+2].
+  // Writes this warp's (o, m, l) for q heads h < group into
+  // merge_w[h][merge_head_floats]: o at [0, HD), (m, l) at HD.
   __device__ __forceinline__ void to_merge(const DecodeArgs& a, float* merge_w, int lane) {
 #pragma unroll
     for (int h = 0; h < GT; ++h) {
@@ -291,17 +295,9 @@ struct F32Consumer {
         ov.w += __shfl_xor_sync(0xffffffffu, ov.w, 16);
       }
       if (h < a.group) {
-        float* mh = merge_w + h * (HD + 2);
-        if (lane < kC4) {
-          mh[lane * 4 + 0] = ov.x;
-          mh[lane * 4 + 1] = ov.y;
-          mh[lane * 4 + 2] = ov.z;
-          mh[lane * 4 + 3] = ov.w;
-        }
-        if (lane == 0) {
-          mh[HD] = m[h];
-          mh[HD + 1] = lt;
-        }
+        float* mh = merge_w + h * merge_head_floats<HD>();
+        if (lane < kC4) *reinterpret_cast<float4*>(mh + lane * 4) = ov;
+        if (lane == 0) *reinterpret_cast<float2*>(mh + HD) = make_float2(m[h], lt);
       }
     }
   }
@@ -489,16 +485,12 @@ struct F16Consumer {
     lt += __shfl_xor_sync(0xffffffffu, lt, 1);
     lt += __shfl_xor_sync(0xffffffffu, lt, 2);
     if (gid < a.group) {
-      float* mh = merge_w + gid * (HD + 2);
+      float* mh = merge_w + gid * merge_head_floats<HD>();
 #pragma unroll
-      for (int nt = 0; nt < kNT; ++nt) {
-        mh[nt * 8 + 2 * tig] = oacc[nt][0] + oacc[nt][2];
-        mh[nt * 8 + 2 * tig + 1] = oacc[nt][1] + oacc[nt][3];
-      }
-      if (tig == 0) {
-        mh[HD] = m_run;
-        mh[HD + 1] = lt;
-      }
+      for (int nt = 0; nt < kNT; ++nt)
+        *reinterpret_cast<float2*>(mh + nt * 8 + 2 * tig) =
+            make_float2(oacc[nt][0] + oacc[nt][2], oacc[nt][1] + oacc[nt][3]);
+      if (tig == 0) *reinterpret_cast<float2*>(mh + HD) = make_float2(m_run, lt);
     }
   }
 };
@@ -745,7 +737,8 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
 
   Consumer cons;
   float* pbuf_w = pbuf + warp * Consumer::kPbufFloats;
-  float* merge_w = merge + warp * kMG * (HD + 2);
+  constexpr int kMH = merge_head_floats<HD>();
+  float* merge_w = merge + warp * kMG * kMH;
   constexpr int kSH = slot_head_floats<HD>();
 
   // The group's q vectors, pre-scaled by scale*log2(e), rows >= G zeroed.
@@ -830,30 +823,35 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
     const int s = b * n_kv + g;
     int32_t c0;
     const int32_t npieces = deal.pieces(seq_start, nunits, b, g, &c0);
-    for (int idx = tid; idx < G * HD; idx += kNCT) {
-      const int h = idx / HD, d = idx - h * HD;
+    // one thread per (head, 4 columns): the warps' (m, l) pairs, then their
+    // o chunks, as float2 / float4 shared loads
+    constexpr int kD4 = HD / 4;
+    for (int idx = tid; idx < G * kD4; idx += kNCT) {
+      const int h = idx / kD4, d = (idx - h * kD4) * 4;
+      float2 ml[NW];
       float M = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < NW; ++w) M = fmaxf(M, merge[(w * kMG + h) * (HD + 2) + HD]);
-      float O = 0.f, L = 0.f;
+      for (int w = 0; w < NW; ++w) {
+        ml[w] = *reinterpret_cast<const float2*>(merge + (w * kMG + h) * kMH + HD);
+        M = fmaxf(M, ml[w].x);
+      }
+      float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+      float L = 0.f;
       if (M != -INFINITY) {
 #pragma unroll
         for (int w = 0; w < NW; ++w) {
-          const float* mh = merge + (w * kMG + h) * (HD + 2);
-          const float sc = fast_exp2(mh[HD] - M);
-          O += sc * mh[d];
-          L += sc * mh[HD + 1];
+          const float4 ow = *reinterpret_cast<const float4*>(merge + (w * kMG + h) * kMH + d);
+          const float sc = fast_exp2(ml[w].x - M);
+          O.x += sc * ow.x; O.y += sc * ow.y; O.z += sc * ow.z; O.w += sc * ow.w;
+          L += sc * ml[w].y;
         }
       }
       if (npieces == 1) {
-        write_final<HD>(a, b, g * G + h, d, O, M, L);
+        write_final4<HD>(a, b, g * G + h, d, O, M, L);
       } else {
         float* slot = a.ws_part + ((int64_t)(blockIdx.x + s) * G + h) * kSH;
-        slot[d] = O;
-        if (d == 0) {
-          slot[HD] = M;
-          slot[HD + 1] = L;
-        }
+        *reinterpret_cast<float4*>(slot + d) = O;
+        if (d == 0) *reinterpret_cast<float2*>(slot + HD) = make_float2(M, L);
       }
     }
     if (npieces > 1) {
