@@ -15,6 +15,8 @@ namespace gla {
 namespace {
 
 constexpr int kTileMax = 64;
+static_assert(F32Consumer<128, 1>::kTileMax == kTileMax && F16Consumer<128>::kTileMax == kTileMax,
+              "consumers address stages with a compile-time tile height");
 
 // consumer warps: FP32 F32Consumer (8), FP16 F16Consumer (4)
 int nw_for(int dtype) { return dtype == GLA_DTYPE_F32 ? 8 : 4; }

@@ -137,23 +137,31 @@ struct F32Consumer {
   static constexpr int kElemBytes = 4;
   static constexpr int kNW = 8;
   static constexpr int kRows = 8;               // rows per warp
-  static constexpr int kTileMax = kRows * kNW;  // 64
+  static constexpr int kTileMax = kRows * kNW;  // 64: the only tile height plans use
   static constexpr int kMergeG = GT;
   static constexpr int kPbufFloats = kRows * 8;  // per warp: 8 rows x 8 heads
   static constexpr int kC4 = HD / 4;             // float4 chunks per row
-  static constexpr int kLP = HD >= 96 ? 8 : 4;   // phase A lanes per row
-  static constexpr int kRL = 32 / kLP;           // phase A rows per pass
-  static constexpr int kPA = kRows / kRL;        // phase A passes
-  static constexpr int kEC = kC4 / kLP;          // phase A chunks per lane and row
-  static constexpr int kRPP = (32 % kC4 == 0) ? 32 / kC4 : 1;  // phase B rows per pass
-  static constexpr int kPasses = kRows / kRPP;
+  // phase A: lane = (row rl of kRL, part of kLP)
+  static constexpr int kLP = HD >= 96 ? 8 : 4;   // lanes per row
+  static constexpr int kRL = 32 / kLP;           // rows per pass
+  static constexpr int kPA = kRows / kRL;        // passes
+  static constexpr int kEC = kC4 / kLP;          // chunks per lane and row
+  // phase B: lane = (row rp of kBR, lane lr of kBL in the row), kBC chunks
+  // lr + j * kBL (interleaved: a quarter warp reads 8 distinct chunks of one
+  // row, conflict-free under the 128-byte swizzle)
+  // (one chunk, one row per pass, when the o accumulators would not fit)
+  static constexpr int kBC = HD == 96 ? (GT <= 3 ? 3 : 1) : (HD == 64 || GT <= 4 ? 2 : 1);
+  static constexpr int kBL = kC4 / kBC;          // lanes per row
+  static constexpr int kBR = 32 / kBL;           // rows per pass (lanes >= kBR * kBL idle)
+  static constexpr int kPB = kRows / kBR;        // passes
   static constexpr int kPH = (GT + 3) / 4;       // float4s of p per row
   static constexpr bool kQReg = GT * kEC * 4 <= 64;
   static_assert(kC4 % kLP == 0, "head_dim must be a multiple of 16 (32 from 96 up)");
-  static_assert(kRPP <= 2, "phase B covers at most two rows per pass");
+  static_assert(kC4 % kBC == 0 && kBL <= 32 && kRows % kBR == 0 &&
+                    (kBR == 1 || kBR * kBL == 32), "phase B lane map");
 
   float m[GT], l[GT];  // m: warp-uniform; l: per-lane part (part-0 lanes own rows)
-  float4 o[GT];        // phase B chunk of each head (half sums when kRPP == 2)
+  float4 o[GT][kBC];   // phase B chunks of each head (sums over this lane's rows)
   float4 qr[kQReg ? GT : 1][kQReg ? kEC : 1];
 
   __device__ __forceinline__ void begin(const DecodeArgs&, const float* qs, int lane) {
@@ -161,7 +169,8 @@ struct F32Consumer {
     for (int h = 0; h < GT; ++h) {
       m[h] = -INFINITY;
       l[h] = 0.f;
-      o[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < kBC; ++j) o[h][j] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     if constexpr (kQReg) {
       const int part = lane / kRL;
@@ -173,13 +182,50 @@ struct F32Consumer {
     }
   }
 
+  template <bool kFull>
+  __device__ __forceinline__ void phase_b(const char* Vs, const float* pbuf_w, int rb, int nvalid,
+                                          int lane) {
+    const bool on = kBR * kBL == 32 || lane < kBL;
+    const int rp = on ? lane / kBL : 0, lr = on ? lane - rp * kBL : 0;
+#pragma unroll
+    for (int pb = 0; pb < kPB; ++pb) {
+      const int r = pb * kBR + rp;
+      float4 vv[kBC];
+#pragma unroll
+      for (int j = 0; j < kBC; ++j) {
+        const float4 t = *reinterpret_cast<const float4*>(
+            Vs + TL::chunk_off(kTileMax, rb + r, (lr + j * kBL) * 4));
+        vv[j] = ((kFull || r < nvalid) && on) ? t : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      const float4* pr = reinterpret_cast<const float4*>(pbuf_w + r * 8);
+#pragma unroll
+      for (int u = 0; u < kPH; ++u) {
+        const float4 pu = pr[u];
+        const float pw[4] = {pu.x, pu.y, pu.z, pu.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int h = 4 * u + e;
+          if (h < GT) {
+#pragma unroll
+            for (int j = 0; j < kBC; ++j) {
+              o[h][j].x = fmaf(pw[e], vv[j].x, o[h][j].x);
+              o[h][j].y = fmaf(pw[e], vv[j].y, o[h][j].y);
+              o[h][j].z = fmaf(pw[e], vv[j].z, o[h][j].z);
+              o[h][j].w = fmaf(pw[e], vv[j].w, o[h][j].w);
+            }
+          }
+        }
+      }
+    }
+  }
+
   __device__ __forceinline__ void consume(const DecodeArgs& a, const char* stage, int rows,
                                           float* pbuf_w, const float* qs, int w, int lane) {
     const int rb = w * kRows;
     if (rb >= rows) return;
     const int rl = lane % kRL, part = lane / kRL;
     const char* Ks = stage;
-    const char* Vs = stage + a.tile * HD * 4;
+    const char* Vs = stage + kTileMax * HD * 4;
     float acc[kPA][GT];
 #pragma unroll
     for (int pa = 0; pa < kPA; ++pa)
@@ -191,7 +237,8 @@ struct F32Consumer {
       float4 k4[kPA];
 #pragma unroll
       for (int pa = 0; pa < kPA; ++pa)
-        k4[pa] = *reinterpret_cast<const float4*>(Ks + TL::chunk_off(a.tile, rb + pa * kRL + rl, c * 4));
+        k4[pa] = *reinterpret_cast<const float4*>(
+            Ks + TL::chunk_off(kTileMax, rb + pa * kRL + rl, c * 4));
 #pragma unroll
       for (int h = 0; h < GT; ++h) {
         float4 q4;
@@ -232,10 +279,13 @@ struct F32Consumer {
       }
       l[h] = l[h] * alpha + (part == 0 ? ps : 0.f);
       m[h] = mn;
-      o[h].x *= alpha;
-      o[h].y *= alpha;
-      o[h].z *= alpha;
-      o[h].w *= alpha;
+#pragma unroll
+      for (int j = 0; j < kBC; ++j) {
+        o[h][j].x *= alpha;
+        o[h][j].y *= alpha;
+        o[h][j].z *= alpha;
+        o[h][j].w *= alpha;
+      }
     }
     if (part == 0) {
 #pragma unroll
@@ -250,55 +300,35 @@ struct F32Consumer {
     }
     __syncwarp();
     const int nvalid = rows - rb;
-    const int sub = kRPP > 1 ? lane / kC4 : 0;
-    const int ch = kRPP > 1 ? lane % kC4 : imin(lane, kC4 - 1);  // lanes >= kC4 idle (hd 96)
-    const bool lane_on = kRPP > 1 || lane < kC4;
-#pragma unroll
-    for (int j = 0; j < kPasses; ++j) {
-      const int r = j * kRPP + sub;
-      const float4 t = *reinterpret_cast<const float4*>(Vs + TL::chunk_off(a.tile, rb + r, ch * 4));
-      const bool ok = lane_on && r < nvalid;
-      const float4 vv = ok ? t : make_float4(0.f, 0.f, 0.f, 0.f);
-      const float4* pr = reinterpret_cast<const float4*>(pbuf_w + r * 8);
-#pragma unroll
-      for (int u = 0; u < kPH; ++u) {
-        const float4 pu = pr[u];
-        const float pw[4] = {pu.x, pu.y, pu.z, pu.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int h = 4 * u + e;
-          if (h < GT) {
-            o[h].x = fmaf(pw[e], vv.x, o[h].x);
-            o[h].y = fmaf(pw[e], vv.y, o[h].y);
-            o[h].z = fmaf(pw[e], vv.z, o[h].z);
-            o[h].w = fmaf(pw[e], vv.w, o[h].w);
-          }
-        }
-      }
-    }
+    if (nvalid >= kRows) phase_b<true>(Vs, pbuf_w, rb, nvalid, lane);
+    else phase_b<false>(Vs, pbuf_w, rb, nvalid, lane);
     __syncwarp();
   }
 
   // Writes this warp's (o, m, l) for q heads h < group into
   // merge_w[h][merge_head_floats]: o at [0, HD), (m, l) at HD.
   __device__ __forceinline__ void to_merge(const DecodeArgs& a, float* merge_w, int lane) {
+    const int rp = lane / kBL, lr = lane - rp * kBL;  // idle lanes (rp >= kBR) write nothing
 #pragma unroll
     for (int h = 0; h < GT; ++h) {
       float lt = l[h];
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, off);
-      float4 ov = o[h];
-      if constexpr (kRPP == 2) {
-        ov.x += __shfl_xor_sync(0xffffffffu, ov.x, 16);
-        ov.y += __shfl_xor_sync(0xffffffffu, ov.y, 16);
-        ov.z += __shfl_xor_sync(0xffffffffu, ov.z, 16);
-        ov.w += __shfl_xor_sync(0xffffffffu, ov.w, 16);
+#pragma unroll
+      for (int j = 0; j < kBC; ++j) {
+        float4 ov = o[h][j];
+#pragma unroll
+        for (int off = kBL; kBR > 1 && off < 32; off <<= 1) {  // join the rows of a pass
+          ov.x += __shfl_xor_sync(0xffffffffu, ov.x, off);
+          ov.y += __shfl_xor_sync(0xffffffffu, ov.y, off);
+          ov.z += __shfl_xor_sync(0xffffffffu, ov.z, off);
+          ov.w += __shfl_xor_sync(0xffffffffu, ov.w, off);
+        }
+        if (h < a.group && rp == 0)
+          *reinterpret_cast<float4*>(merge_w + h * merge_head_floats<HD>() + (lr + j * kBL) * 4) = ov;
       }
-      if (h < a.group) {
-        float* mh = merge_w + h * merge_head_floats<HD>();
-        if (lane < kC4) *reinterpret_cast<float4*>(mh + lane * 4) = ov;
-        if (lane == 0) *reinterpret_cast<float2*>(mh + HD) = make_float2(m[h], lt);
-      }
+      if (h < a.group && lane == 0)
+        *reinterpret_cast<float2*>(merge_w + h * merge_head_floats<HD>() + HD) = make_float2(m[h], lt);
     }
   }
 };
