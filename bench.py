@@ -74,9 +74,9 @@ def peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def traffic_from_profiles(workload):
+def traffic_from_profiles(workload, kernel="decode_kernel"):
     """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
-    path = os.path.join(REPO, "profiles", f"decode_kernel_{workload}.md")
+    path = os.path.join(REPO, "profiles", f"{kernel}_{workload}.md")
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):
@@ -496,6 +496,47 @@ def ms_est(fn, stream, torch, device):
     return e0.elapsed_time(e1)
 
 
+def cpu_prefill_sample(wl, budget_s=8.0):
+    """CPU prefill baseline.  The reference ingests a prompt one position at a
+    time (InferenceEngine.java:88-99: decode attention over rows 0..p for every
+    p), in FP32.  A spread of 16 positions is timed with the oracle (its C
+    restatement) on the FP16-rounded inputs and the time is scaled by row
+    count to the whole causal triangle."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle  # test infrastructure: timed CPU baseline only
+
+    oracle.build()
+    L, nh, nkv, hd = wl["T"], wl["n_heads"], wl["n_kv"], wl["hd"]
+    threads = min(nh, oracle.max_threads())
+    rng = np.random.Generator(np.random.PCG64(0))
+    q = rng.standard_normal((L, nh * hd), dtype=np.float32).astype(np.float16).astype(np.float32)
+    k = rng.standard_normal((L, nkv * hd), dtype=np.float32).astype(np.float16).astype(np.float32)
+    v = rng.standard_normal((L, nkv * hd), dtype=np.float32).astype(np.float16).astype(np.float32)
+    positions = [int(x) for x in np.linspace(0, L - 1, 16)]
+    visits = sum(p + 1 for p in positions)
+
+    def sweep():
+        for p in positions:
+            oracle.decode_f32(q[p], k, v, nh, nkv, hd, p + 1, n_threads=threads)
+
+    sweep()  # warm-up
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while True:
+        t0 = time.perf_counter()
+        sweep()
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end and len(times) >= 3:
+            break
+    full_s = statistics.median(times) / visits * (L * (L + 1) / 2)
+    flops = 4.0 * nh * hd * L * (L + 1) / 2
+    return dict(value=round(flops / full_s / 1e12, 6), unit="TFLOP/s", cores=threads,
+                kind="port",
+                sample=f"{len(positions)} prompt positions spread over 0..{L - 1}, "
+                       f"median of {len(times)} sweeps, scaled by row count to all "
+                       f"{L} positions ({full_s:.1f} s per prompt)")
+
+
 def run_prefill(args, rank, world, local_rank, dist):
     """causal prefill, L 4096, 32 heads, hd 96, FP16 in, FP32
     softmax/accumulation/out. Metric: causal TFLOP/s = 4*nH*hd*L(L+1)/2 / time."""
@@ -606,7 +647,8 @@ def run_prefill(args, rank, world, local_rank, dist):
                    "parallelism": f"replicas{world}" if world > 1 else "single"},
         "gpu_launches": args.steps,
         "roofline": {"bound": "tensor", "achieved": round(tflops / world, 2), "peak": peak,
-                     "unit": "TFLOP/s", "frac": round(tflops / world / peak, 4), "traffic": None,
+                     "unit": "TFLOP/s", "frac": round(tflops / world / peak, 4),
+                     "traffic": traffic_from_profiles("c5", "prefill_kernel"),
                      "peak_source": peak_kind, "kernel": "gla::prefill_kernel<96>",
                      "flops_per_launch": flops},
         "clocks": dict(clocks, soak_s=round(soak_s, 2)) if clocks else None,
@@ -615,6 +657,8 @@ def run_prefill(args, rank, world, local_rank, dist):
                 "h2d_bytes_per_step": int((q.numel() + k.numel() + v.numel()) * 2),
                 "d2h_bytes_per_step": int(out.numel() * 4)},
     }
+    if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.quick):
+        res["cpu_baseline"] = cpu_prefill_sample(wl)
     ctx.close()
     return res
 
@@ -686,8 +730,40 @@ def run_e2e(args, ctx, wl, inp, torch, device, stream, dist):
 # ---------------------------------------------------------------------------
 # Reference arm: the reference's CPU attention (C restatement) on host cores
 # ---------------------------------------------------------------------------
+def run_reference_prefill(args, world):
+    wl = WORKLOADS["c5"]
+    L, nh, hd = wl["T"], wl["n_heads"], wl["hd"]
+    flops = 4.0 * nh * hd * L * (L + 1) / 2
+    values = []
+    base = None
+    for i in range(max(0, args.warmup) + args.steps):
+        base = cpu_prefill_sample(wl, budget_s=2.0)
+        if i >= args.warmup:
+            values.append(base["value"])
+    value = statistics.mean(values)
+    ms = flops / (value * 1e12) * 1e3
+    return {
+        "metric": "prefill-attn TFLOP/s (causal)", "value": round(value, 6), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic ~N(0,1), numpy PCG64 seed 0",
+        "config": {"workload": wl["name"], "baseline_config": "c5", "L": L, "n_heads": nh,
+                   "n_kv_heads": wl["n_kv"], "head_dim": hd, "causal": True},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": base["cores"],
+                         "kind": "port", "sample": base["sample"]},
+        "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "the reference ingests prompts position by position in Java "
+                "(InferenceEngine.java:88-99); no JDK exists on this box, so its C "
+                "restatement (oracle/) is timed on a sample of positions",
+    }
+
+
 def run_reference(args, rank, world):
     wl = WORKLOADS[args.workload]
+    if args.workload == "c5":
+        return run_reference_prefill(args, world)
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import oracle  # the reference's CPU path, restated
 

@@ -6,20 +6,25 @@
 // time while it ingests a prompt (InferenceEngine.java:88-99, one
 // InferenceCore.forwardJava attention block per position).
 //
-// One CTA per (head, 128-row query block), heaviest blocks first:
-//   warp 4     producer: TMA loads of the Q block once, then K and V blocks of
-//              128 keys into two separate rings (SWIZZLE_64B, 32-half column
-//              blocks): K_j is released as soon as S_j is computed, V_j after
-//              P_j V_j, so the next K tiles stream in while softmax runs.
-//   warp 5     MMA issuer (one thread): S_j = Q K_j^T into TMEM (double
-//              buffered, 128 columns each), then O += P_j V_j into a TMEM
-//              accumulator; tcgen05.commit signals mbarriers.
-//   warps 0-3  softmax: thread r owns query row r, reads its 128 scores with
-//              tcgen05.ld, keeps the row max/sum in registers (no shuffles),
-//              writes P_j (FP16) to a swizzled shared-memory buffer for the
-//              second MMA, and rescales O in TMEM only when the row max grows
-//              by more than 2^8 (otherwise p <= 2^8 stays exact in FP16 and
-//              the final division by l absorbs the stale max).
+// One CTA per (head, block of NT 128-row query tiles), heaviest blocks first
+// (NT = 2 for head_dim 64/96, 1 for 128); 4 NT + 2 warps:
+//   warp 4NT   producer: TMA loads of the NT Q tiles once, then K and V
+//              blocks of 128 keys into two separate rings (SWIZZLE_64B,
+//              32-half column blocks): K_j is released as soon as every S of
+//              block j is computed, V_j after the P V products, so the next
+//              K tiles stream in while softmax runs.
+//   warp 4NT+1 MMA issuer (one thread): per query tile t, S_t = Q_t K_j^T
+//              into TMEM columns [256t, 256t+128), then O_t += P_t V_j into
+//              columns [256t+128, 256t+128+hd); the tiles alternate, so one
+//              tile's MMAs run while the other tile's softmax works;
+//              tcgen05.commit signals mbarriers.
+//   warps 4t..4t+3, softmax of query tile t: thread r owns query row r,
+//              reads its 128 scores with tcgen05.ld in two 64-column passes,
+//              keeps the row max/sum in registers (no shuffles), writes P
+//              (FP16) to a swizzled shared-memory buffer for the second MMA,
+//              and rescales O in TMEM only when the row max grows by more
+//              than 2^8 (otherwise p <= 2^8 stays exact in FP16 and the final
+//              division by l absorbs the stale max).
 // FP32 softmax and accumulation; FP16 inputs; FP32 output.
 #include <cudaTypedefs.h>
 
