@@ -30,7 +30,7 @@ struct gla_ctx {
   float* gathered = nullptr;        // sharded decode: all ranks' records
   size_t records_cap = 0;           // floats per rank
   gla::Comm comm;
-  int32_t opt_early_kv = 1;         // GLA_OPT_EARLY_KV_PREFETCH
+  int32_t opt_early_kv = 2;         // GLA_OPT_EARLY_KV_PREFETCH
   std::string last_error;
 };
 
@@ -390,7 +390,8 @@ int32_t gla_set_option(gla_ctx* ctx, int32_t option, int32_t value) {
   if (!ctx) return GLA_ERR_INVALID_ARG;
   switch (option) {
     case GLA_OPT_EARLY_KV_PREFETCH:
-      ctx->opt_early_kv = value ? 1 : 0;
+      if (value < 0 || value > 2) return fail(ctx, GLA_ERR_INVALID_ARG, "value must be 0, 1 or 2");
+      ctx->opt_early_kv = value;
       return GLA_OK;
     default:
       return fail(ctx, GLA_ERR_INVALID_ARG, "unknown option");

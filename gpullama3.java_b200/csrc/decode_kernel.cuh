@@ -54,8 +54,8 @@ struct DecodeArgs {
   int32_t n_pos_add;           // added to n_pos_dev[b] (position holder: +1)
   int32_t n_pos_cap;           // rows present in the cache; larger n_pos is clamped
                                // and latched as GLA_ERR_INVALID_ARG
-  int32_t early_kv;            // LOADER 0, host n_pos: prefetch history tiles before
-                               // the preceding grid completes (see kernel)
+  int32_t early_kv;            // LOADER 0: prefetch history tiles before the preceding
+                               // grid completes: 1 host n_pos, 2 also n_pos_dev (see kernel)
   int32_t batch;
   int32_t n_heads;
   int32_t n_kv;
@@ -650,18 +650,21 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
       tma_load_2d(vs + off, &a.tmap_v, x, t.row0, &full[st], pol);
     }
   };
-  // Early KV prefetch (programmatic dependent launch).  With a host n_pos the
-  // work partition needs no memory, so the producer may start streaming this
-  // CTA's first tiles while the preceding kernel on the stream drains.  Only
-  // tiles holding cache history (rows < n_pos - 1) are fetched early: the
-  // newest row is the one a KV append kernel may have just written.  Decode
-  // kernels (the only kernels here that release dependents early) never write
-  // a cache; a preceding kernel that does not release dependents has finished
-  // before this grid starts.
+  // Early KV prefetch (programmatic dependent launch).  The work partition
+  // needs only the positions, so the producer may start streaming this CTA's
+  // first tiles while the preceding kernel on the stream drains: with a host
+  // n_pos (early_kv >= 1), or with positions read from the device
+  // (early_kv == 2: the caller vouches that a kernel releasing its
+  // dependents early does not write them).  Only tiles holding cache history
+  // (rows < n_pos - 1) are fetched early: the newest row is the one a KV
+  // append kernel may have just written.  Decode kernels (the only kernels
+  // here that release dependents early) never write a cache or a position; a
+  // preceding kernel that does not release dependents has finished before
+  // this grid starts.
   // The ring's first pass (up to `stages` tiles) is walked here; a tile
   // holding a sequence's newest row is skipped (bit k of `late`) and fetched
   // after the wait, the tiles behind it are not held back.
-  const bool early = LOADER == 0 && a.early_kv && a.n_pos_dev == nullptr;
+  const bool early = LOADER == 0 && (a.n_pos_dev == nullptr ? a.early_kv >= 1 : a.early_kv >= 2);
   int32_t n_early = 0;
   uint32_t late = 0;
   if (early) {

@@ -30,7 +30,7 @@ struct DecodeRequest {
   float scale;
   float* out;
   int32_t record_mode;
-  int32_t early_kv;            // GLA_OPT_EARLY_KV_PREFETCH (host n_pos calls only)
+  int32_t early_kv;            // GLA_OPT_EARLY_KV_PREFETCH value (0, 1 or 2)
 };
 
 // Launch geometry chosen for a request.

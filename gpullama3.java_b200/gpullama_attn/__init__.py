@@ -24,7 +24,7 @@ DTYPE_F32 = 0
 DTYPE_F16 = 1
 ROPE_INTERLEAVED = 0
 ROPE_NEOX = 1
-OPT_EARLY_KV_PREFETCH = 1
+OPT_EARLY_KV_PREFETCH = 1  # values: 0 off, 1 host n_pos, 2 (default) also device positions
 
 STATUS_NAMES = {
     0: "GLA_OK", -1: "GLA_ERR_INVALID_ARG", -2: "GLA_ERR_CUDA", -3: "GLA_ERR_NOT_SUPPORTED",

@@ -93,14 +93,23 @@ int32_t gla_num_sms(const gla_ctx* ctx);
 
 /* Context options (gla_set_option). */
 #define GLA_OPT_EARLY_KV_PREFETCH 1
-/* GLA_OPT_EARLY_KV_PREFETCH (default 1): decode calls that take n_pos from
- * the host (gla_decode_*, gla_decode_partial_*, gla_decode_sharded_*) launch
- * with programmatic dependent launch and may start reading K/V rows
- * [0, n_pos - 1) - the cache history - before the kernel issued just before
- * them on the stream has finished.  The newest row (n_pos - 1), q and every
- * other input are read only after it has finished.  Set 0 if a kernel that
- * runs right before a decode call, and releases its dependents early
- * (griddepcontrol.launch_dependents), writes older cache rows. */
+/* GLA_OPT_EARLY_KV_PREFETCH (default 2).  Decode calls launch with
+ * programmatic dependent launch and may start reading before the kernel
+ * issued just before them on the stream has finished - only if that kernel
+ * releases its dependents early (griddepcontrol.launch_dependents); the
+ * decode kernels of this library do, and never write caches or positions.
+ * What may be read early:
+ *   1 - calls that take n_pos from the host (gla_decode_*,
+ *       gla_decode_partial_*, gla_decode_sharded_*): K/V rows
+ *       [0, n_pos - 1), the cache history;
+ *   2 - also calls that read positions on the device
+ *       (gla_process_heads_flash_attention*, gla_decode_batched_*): the
+ *       position holder / n_pos array, then the history rows below it.
+ * The newest row (n_pos - 1), q and every other input are read only after
+ * the preceding kernel has finished.  0 turns early reads off.  Lower the
+ * value if a kernel that runs right before a decode call and releases its
+ * dependents early writes older cache rows (use 0) or the positions (use 1).
+ * (Early reads apply to the tensor-map loader: single-sequence calls.) */
 int32_t gla_set_option(gla_ctx* ctx, int32_t option, int32_t value);
 
 /* ------------------------------------------------------------------------ */

@@ -307,22 +307,31 @@ def test_early_prefetch_sees_the_row_appended_just_before(gla_ctx, oracle):
     vnew = rng.standard_normal(nkv * hd, dtype=np.float32)
     k[pos] = 7.0  # stale row contents the append must replace
     v[pos] = -7.0
-    outs = []
-    for opt in (1, 0):
+    outs, outs_dev = [], []
+    for opt in (2, 1, 0):
         gla_ctx.set_option(gla.OPT_EARLY_KV_PREFETCH, opt)
         kc, vc = dev(k), dev(v)
         qd, kd, vd = dev(q0), dev(knew), dev(vnew)
         ph = torch.tensor([pos], dtype=torch.int32, device="cuda")
         xb = torch.empty(nh * hd, device="cuda")
+        xb2 = torch.empty(nh * hd, device="cuda")
         for _ in range(3):  # back-to-back decodes: PDL overlap between them
             gla_ctx.decode(qd, kc, vc, xb, nh, nkv, hd, pos)
         gla_ctx.rope_append(qd, kd, vd, kc, vc, nh, nkv, hd, ph, 500000.0)
         gla_ctx.decode(qd, kc, vc, xb, nh, nkv, hd, pos + 1)
+        # the device-position path right behind a decode (PDL overlap), as a
+        # layer plan issues it: position holder = pos, rows 0..pos
+        gla_ctx.process_heads_flash_attention(qd, kc, vc, xb2, nh, hd, nkv * hd, nh // nkv, ph,
+                                              0, T)
         assert gla_ctx.device_status() == 0
         outs.append(xb.cpu().numpy())
+        outs_dev.append(xb2.cpu().numpy())
         kk, vv, qq = kc.cpu().numpy(), vc.cpu().numpy(), qd.cpu().numpy()
         ref = oracle.decode_f32(qq, kk, vv, nh, nkv, hd, pos + 1)
         assert_close(outs[-1], ref, TOL_F32, f"option {opt}")
+        assert_close(outs_dev[-1], ref, TOL_F32, f"option {opt}, device position")
         assert np.abs(kk[pos]).max() < 7.0 and vv[pos][0] == vnew[0]
-    gla_ctx.set_option(gla.OPT_EARLY_KV_PREFETCH, 1)
+    gla_ctx.set_option(gla.OPT_EARLY_KV_PREFETCH, 2)
     np.testing.assert_array_equal(outs[0], outs[1])
+    np.testing.assert_array_equal(outs[0], outs[2])
+    np.testing.assert_array_equal(outs_dev[0], outs_dev[2])
