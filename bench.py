@@ -332,7 +332,7 @@ def run_ours(args, rank, world, local_rank, dist):
             elif args.workload == "c4" and world > 1:
                 ctx.decode_sharded(inp["q"][l], inp["K"][l], inp["V"][l], xb[l], nh, nkv, hd,
                                    n_local, f16_cache=True)
-                n += 2
+                n += 1 if ctx.peer_exchange else 2
             else:
                 ctx.decode(inp["q"][l], inp["K"][l], inp["V"][l], xb[l], nh, nkv, hd,
                            inp["K"].shape[1], f16_cache=wl["f16"])
@@ -349,7 +349,9 @@ def run_ours(args, rank, world, local_rank, dist):
         raise RuntimeError(f"device status {st} after warm-up")
 
     graph = None
-    use_graph = not (args.workload == "c4" and world > 1)  # NCCL calls stay eager
+    peer = args.workload == "c4" and world > 1 and ctx.peer_exchange
+    # the NCCL path stays eager; the peer exchange is one kernel and is captured
+    use_graph = not (args.workload == "c4" and world > 1) or peer
     if use_graph:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
@@ -411,9 +413,10 @@ def run_ours(args, rank, world, local_rank, dist):
         e2e = run_e2e(args, ctx, wl, inp, torch, device, stream, dist)
 
     # dominant kernel's average duration: the timed region holds only decode
-    # launches except for sharded c4, whose partial kernel is timed on its own
+    # launches except for sharded c4 over NCCL, whose partial kernel is timed
+    # on its own (on the peer exchange the step is one fused kernel)
     per_launch_ms = ms / max(1, launches_per_step)
-    if args.workload == "c4" and world > 1:
+    if args.workload == "c4" and world > 1 and not peer:
         part = torch.empty(nh, hd + 2, device=device)
         with torch.cuda.stream(stream):
             for _ in range(args.warmup):
@@ -460,7 +463,9 @@ def run_ours(args, rank, world, local_rank, dist):
                    "kv_dtype": "f16" if wl["f16"] else "f32", "global_batch": wl["batch"] *
                    (world if args.workload in ("c1", "c2") else 1),
                    "parallelism": (f"seq-shard{world}" if args.workload != "c4" else
-                                   f"kv-shard{world}+nccl-allgather") if world > 1 else "single",
+                                   f"kv-shard{world}+" + ("peer-exchange" if peer else
+                                                          "nccl-allgather"))
+                                  if world > 1 else "single",
                    "l2": "inputs exceed L2 (KV bytes per launch > 126 MB L2)"
                    if bytes_step / world / max(1, L) > 126e6 else
                    ("inputs exceed L2 (KV bytes per step > 126 MB; layers rotate)"

@@ -16,6 +16,8 @@
 #include "gla_common.cuh"
 #include "gla_internal.h"
 #include "gla_comm.h"
+#include "gla_peer.h"
+#include "gla_xch.h"
 
 struct gla_ctx {
   int device = 0;
@@ -30,7 +32,9 @@ struct gla_ctx {
   float* gathered = nullptr;        // sharded decode: all ranks' records
   size_t records_cap = 0;           // floats per rank
   gla::Comm comm;
+  gla::PeerExchange xch;            // sharded decode: peer exchange buffers
   int32_t opt_early_kv = 2;         // GLA_OPT_EARLY_KV_PREFETCH
+  int32_t opt_shard_exchange = 1;   // GLA_OPT_SHARD_EXCHANGE
   std::string last_error;
 };
 
@@ -258,6 +262,43 @@ int sharded(gla_ctx* ctx, int dtype, const float* q, const void* k, const void* 
     ctx->records_cap = rec;
   }
   int rc;
+  if (ctx->opt_shard_exchange && ctx->xch.active() && rec <= (size_t)gla::kXchRecFloats &&
+      n_kv_heads <= gla::kXchMaxSeg) {
+    // one kernel: shard attention, records to every rank over peer memory,
+    // merge; an empty shard (n_pos_local == 0) still publishes empty records
+    if (!q || !k || !v) return fail(ctx, GLA_ERR_INVALID_ARG, "null tensor pointer");
+    if (n_pos_local < 0) return fail(ctx, GLA_ERR_INVALID_ARG, "n_pos_local must be >= 0");
+    if (!std::isfinite(scale)) return fail(ctx, GLA_ERR_INVALID_ARG, "scale must be finite");
+    const int esize = dtype == GLA_DTYPE_F32 ? 4 : 2;
+    rc = check_decode_shape(ctx, n_heads, n_kv_heads, head_dim, kv_stride, esize);
+    if (rc != GLA_OK) return rc;
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(xb))
+      return fail(ctx, GLA_ERR_ALIGNMENT, "q, k, v and xb must be 16-byte aligned");
+    DeviceGuard dg(ctx->device);
+    gla::DecodeRequest req{};
+    req.dtype = dtype;
+    req.q = q;
+    req.k = k;
+    req.v = v;
+    req.kv_stride = kv_stride;
+    req.n_pos = n_pos_local;
+    req.n_pos_cap = std::max(1, n_pos_local);
+    req.max_n_pos = n_pos_local;
+    req.batch = 1;
+    req.n_heads = n_heads;
+    req.n_kv = n_kv_heads;
+    req.head_dim = head_dim;
+    req.scale = scale;
+    req.out = ctx->records;
+    req.record_mode = 2;
+    req.early_kv = ctx->opt_early_kv;
+    req.xch_bases = ctx->xch.bases();
+    req.xch_local = ctx->xch.local();
+    req.xch_out = xb;
+    req.xch_world = ctx->xch.world;
+    req.xch_rank = ctx->xch.rank;
+    return run_decode(ctx, req);
+  }
   if (n_pos_local >= 1) {
     rc = decode_single(ctx, dtype, q, k, v, ctx->records, n_heads, n_kv_heads, head_dim, kv_stride,
                        n_pos_local, scale, 1);
@@ -336,6 +377,7 @@ int32_t gla_destroy(gla_ctx* ctx) {
   {
     DeviceGuard dg(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    ctx->xch.teardown();
     ctx->comm.destroy();
     cudaFree(ctx->status);
     cudaFree(ctx->counters);
@@ -389,6 +431,10 @@ int32_t gla_num_sms(const gla_ctx* ctx) { return ctx ? ctx->dev.sms : 0; }
 int32_t gla_set_option(gla_ctx* ctx, int32_t option, int32_t value) {
   if (!ctx) return GLA_ERR_INVALID_ARG;
   switch (option) {
+    case GLA_OPT_SHARD_EXCHANGE:
+      if (value < 0 || value > 1) return fail(ctx, GLA_ERR_INVALID_ARG, "value must be 0 or 1");
+      ctx->opt_shard_exchange = value;
+      return GLA_OK;
     case GLA_OPT_EARLY_KV_PREFETCH:
       if (value < 0 || value > 2) return fail(ctx, GLA_ERR_INVALID_ARG, "value must be 0, 1 or 2");
       ctx->opt_early_kv = value;
@@ -526,8 +572,18 @@ int32_t gla_comm_init(gla_ctx* ctx, int32_t nranks, int32_t rank, const void* un
     return fail(ctx, GLA_ERR_INVALID_ARG, "bad communicator arguments");
   DeviceGuard dg(ctx->device);
   std::string err;
+  ctx->xch.teardown();
   int rc = ctx->comm.init(nranks, rank, unique_id, &err);
-  return rc == GLA_OK ? GLA_OK : fail(ctx, rc, err);
+  if (rc != GLA_OK) return fail(ctx, rc, err);
+  if (ctx->opt_shard_exchange && nranks > 1) {
+    rc = ctx->xch.setup(ctx->comm, ctx->stream, &err);
+    if (rc != GLA_OK) return fail(ctx, rc, err);
+  }
+  return GLA_OK;
+}
+
+int32_t gla_comm_peer_exchange(const gla_ctx* ctx) {
+  return ctx && ctx->opt_shard_exchange && ctx->xch.active() ? 1 : 0;
 }
 
 int32_t gla_decode_sharded_f16kv(gla_ctx* ctx, const float* q, const uint16_t* k,

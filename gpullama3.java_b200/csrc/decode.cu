@@ -260,6 +260,11 @@ int launch_decode(const DecodeRequest& r, const DecodePlan& p, float* ws_part, i
   a.q_scale = r.scale * 1.4426950408889634f;
   a.out = r.out;
   a.record_mode = r.record_mode;
+  a.xch_bases = r.xch_bases;
+  a.xch_local = r.xch_local;
+  a.xch_out = r.xch_out;
+  a.xch_world = r.xch_world;
+  a.xch_rank = r.xch_rank;
   a.ws_part = ws_part;
   a.ws_counter = ws_counter;
   a.status = status;

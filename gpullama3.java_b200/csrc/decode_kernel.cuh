@@ -37,6 +37,7 @@
 #pragma once
 
 #include "gla_common.cuh"
+#include "gla_xch.h"
 
 namespace gla {
 
@@ -64,7 +65,14 @@ struct DecodeArgs {
   int32_t stages;
   float q_scale;               // scale * log2(e)
   float* out;                  // xb [B][n_heads][HD] or records [B][n_heads][HD+2]
-  int32_t record_mode;
+  int32_t record_mode;         // 0 xb, 1 records, 2 records merged across ranks (peer
+                               // exchange, one sequence; see gla_xch.h)
+  const uint64_t* xch_bases;   // mode 2: device [world], every rank's exchange buffer as
+                               // mapped in this process
+  char* xch_local;             // mode 2: this rank's exchange buffer
+  float* xch_out;              // mode 2: merged xb [n_heads][HD]
+  int32_t xch_world;
+  int32_t xch_rank;
   float* ws_part;              // workspace slots [P + B*n_kv][G][HD+4] (o, m, l, pad)
   int32_t* ws_counter;         // [B*n_kv], zero between calls
   int32_t* status;             // device status word
@@ -599,6 +607,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
     }
     flags[0] = 0;
     flags[1] = 0;
+    flags[2] = 0;
     fence_mbarrier_init();
   }
   if (LOADER == 0 && warp == NW && lane == 0) {
@@ -690,6 +699,10 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   pdl_wait();
   pdl_launch_dependents();
   if (!early) scan_sequences();
+  // peer exchange: this call's epoch (calls completed on this rank + 1), read
+  // once per CTA after the wait (the previous call's last CTA advances it)
+  if (a.record_mode == 2 && tid == 0)
+    flags[2] = (int)(*reinterpret_cast<volatile uint32_t*>(a.xch_local + xch_epoch_offset()) + 1u);
   __syncthreads();
 
   const int32_t W = seq_start[B];
@@ -759,14 +772,101 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   }
 
   // ---------------- consumers ----------------
+  // Peer exchange (record_mode 2, one sequence): the finished records of kv
+  // head g (written to a.out by this CTA's threads) go to slot [parity][own
+  // rank] of every rank's exchange buffer with plain peer stores; after a
+  // system fence one thread raises flag [parity][own rank][g] on every rank.
+  // Then every rank's flag for g is awaited in this rank's buffer (bounded:
+  // a missing rank latches GLA_ERR_TIMEOUT) and the world records of g are
+  // merged into xb: M = max m_r, w_r = l_r e^(m_r - M),
+  // xb = sum w_r o_r / sum w_r.
+  auto publish_merge = [&](int g) {
+    const uint32_t ep = (uint32_t)flags[2];
+    const int par = (int)(ep & 1u), W = a.xch_world, me = a.xch_rank;
+    const int nf = G * (HD + 2);
+    const float* src = a.out + (int64_t)g * G * (HD + 2);
+    for (int r = 0; r < W; ++r) {
+      float* dst = reinterpret_cast<float*>(a.xch_bases[r] + xch_rec_offset(par, me)) +
+                   (int64_t)g * G * (HD + 2);
+      for (int i = tid; i < nf; i += kNCT) dst[i] = src[i];
+    }
+    consumer_sync(kNCT);
+    if (tid == 0) {
+      __threadfence_system();
+      for (int r = 0; r < W; ++r)
+        st_relaxed_sys_u32(reinterpret_cast<uint32_t*>(a.xch_bases[r] + xch_flag_offset(par, me, g)),
+                           ep);
+    }
+    if (tid < W) {
+      const uint32_t* f = reinterpret_cast<const uint32_t*>(a.xch_local + xch_flag_offset(par, tid, g));
+      if (ld_acquire_sys_u32(f) != ep) {
+        const unsigned long long t0 = global_timer_ns();
+        while (ld_acquire_sys_u32(f) != ep) {
+          if (flags[0]) break;
+          if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+            flags[0] = 1;
+            atomicCAS(a.status, 0, GLA_ERR_TIMEOUT);
+            break;
+          }
+        }
+      }
+    }
+    consumer_sync(kNCT);
+    for (int idx = tid; idx < G * HD; idx += kNCT) {
+      const int hq = g * G + idx / HD, d = idx % HD;
+      float M = -INFINITY;
+      for (int r = 0; r < W; ++r) {
+        const float* rec = reinterpret_cast<const float*>(a.xch_local + xch_rec_offset(par, r)) +
+                           (int64_t)hq * (HD + 2);
+        if (ld_cg(rec + HD + 1) > 0.f) M = fmaxf(M, ld_cg(rec + HD));
+      }
+      float O = 0.f, L = 0.f;
+      if (M != -INFINITY) {
+        for (int r = 0; r < W; ++r) {
+          const float* rec = reinterpret_cast<const float*>(a.xch_local + xch_rec_offset(par, r)) +
+                             (int64_t)hq * (HD + 2);
+          const float l = ld_cg(rec + HD + 1);
+          if (l > 0.f) {
+            const float w = l * __expf(ld_cg(rec + HD) - M);
+            O += w * ld_cg(rec + d);
+            L += w;
+          }
+        }
+      }
+      a.xch_out[(int64_t)hq * HD + d] = L > 0.f ? O / L : 0.f;
+    }
+    consumer_sync(kNCT);
+  };
+  // Peer exchange: the last CTA of the call to finish advances the epoch.
+  auto cta_exit = [&]() {
+    if (a.record_mode != 2) return;
+    consumer_sync(kNCT);
+    if (tid == 0) {
+      int32_t* done = reinterpret_cast<int32_t*>(a.xch_local + xch_done_offset());
+      if (atomic_add_acq_rel_gpu(done, 1) == (int)gridDim.x - 1) {
+        *reinterpret_cast<volatile int32_t*>(done) = 0;
+        *reinterpret_cast<volatile uint32_t*>(a.xch_local + xch_epoch_offset()) =
+            (uint32_t)flags[2];
+      }
+    }
+  };
+
   // segments with no rows (n_pos <= 0) produce zeros / empty records
   for (int s = blockIdx.x; s < B * n_kv; s += gridDim.x) {
     const int b = s / n_kv, g = s - b * n_kv;
-    if (nunits[b] == 0)
+    if (nunits[b] == 0) {
       for (int idx = tid; idx < G * HD; idx += kNCT)
         write_final<HD>(a, b, g * G + idx / HD, idx % HD, 0.f, 0.f, 0.f);
+      if (a.record_mode == 2) {
+        consumer_sync(kNCT);
+        publish_merge(g);
+      }
+    }
   }
-  if (my_count == 0) return;
+  if (my_count == 0) {
+    cta_exit();
+    return;
+  }
 
   Consumer cons;
   float* pbuf_w = pbuf + warp * Consumer::kPbufFloats;
@@ -887,6 +987,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
         if (d == 0) *reinterpret_cast<float2*>(slot + HD) = make_float2(M, L);
       }
     }
+    bool merged_here = npieces == 1;  // this CTA holds the segment's final records
     if (npieces > 1) {
       consumer_sync(kNCT);
       if (tid == 0) {
@@ -894,12 +995,14 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
         flags[1] = (old == npieces - 1) ? 1 : 0;
       }
       consumer_sync(kNCT);
-      if (flags[1]) {
+      merged_here = flags[1] != 0;
+      if (merged_here) {
         combine_pieces(b, g, s, c0, npieces);
         if (tid == 0) a.ws_counter[s] = 0;
       }
     }
     consumer_sync(kNCT);
+    if (a.record_mode == 2 && merged_here) publish_merge(g);
   };
 
   // Piece by piece, tile by tile: the inner loop carries only the ring
@@ -927,6 +1030,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
     }
     finish_piece(pc.b, pc.g);
   }
+  cta_exit();
 }
 
 }  // namespace gla

@@ -350,6 +350,17 @@ __device__ __forceinline__ int atomic_add_acq_rel_gpu(int32_t* p, int v) {
   return old;
 }
 
+// System-scope flag accesses for the peer exchange (another GPU's kernel
+// writes or reads the word over NVLink).
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // Programmatic dependent launch: wait for the preceding grid's memory, and
 // let the next grid start its prologue early.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

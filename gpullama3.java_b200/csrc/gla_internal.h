@@ -31,6 +31,12 @@ struct DecodeRequest {
   float* out;
   int32_t record_mode;
   int32_t early_kv;            // GLA_OPT_EARLY_KV_PREFETCH value (0, 1 or 2)
+  // record_mode 2 (peer exchange of a sharded sequence; gla_xch.h)
+  const uint64_t* xch_bases = nullptr;  // device [world]
+  char* xch_local = nullptr;
+  float* xch_out = nullptr;
+  int32_t xch_world = 0;
+  int32_t xch_rank = 0;
 };
 
 // Launch geometry chosen for a request.

@@ -25,6 +25,7 @@ DTYPE_F16 = 1
 ROPE_INTERLEAVED = 0
 ROPE_NEOX = 1
 OPT_EARLY_KV_PREFETCH = 1  # values: 0 off, 1 host n_pos, 2 (default) also device positions
+OPT_SHARD_EXCHANGE = 2     # 1 (default): peer exchange when available, 0: NCCL all-gather
 
 STATUS_NAMES = {
     0: "GLA_OK", -1: "GLA_ERR_INVALID_ARG", -2: "GLA_ERR_CUDA", -3: "GLA_ERR_NOT_SUPPORTED",
@@ -74,6 +75,7 @@ _SIGS = {
     "gla_rope_append_f32": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P, _F, _I32]),
     "gla_debug_partition": (_I64, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P,
                                    _P, _P, _I64]),
+    "gla_comm_peer_exchange": (_I32, [_P]),
     "gla_decode_f32kv_noalloc": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F, _P]),
 }
 
@@ -268,6 +270,11 @@ class Context:
     def comm_init(self, nranks: int, rank: int, unique_id: bytes):
         buf = ctypes.create_string_buffer(unique_id, len(unique_id))
         self._check(self._L.gla_comm_init(self._h, nranks, rank, buf), "gla_comm_init")
+
+    @property
+    def peer_exchange(self) -> bool:
+        """True if sharded decode merges over the peer exchange (else NCCL)."""
+        return bool(self._L.gla_comm_peer_exchange(self._h))
 
     def decode_sharded(self, q, k, v, xb, n_heads, n_kv_heads, head_dim, n_pos_local,
                        scale=None, kv_stride=None, f16_cache=True):

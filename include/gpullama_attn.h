@@ -110,6 +110,11 @@ int32_t gla_num_sms(const gla_ctx* ctx);
  * value if a kernel that runs right before a decode call and releases its
  * dependents early writes older cache rows (use 0) or the positions (use 1).
  * (Early reads apply to the tensor-map loader: single-sequence calls.) */
+#define GLA_OPT_SHARD_EXCHANGE 2
+/* GLA_OPT_SHARD_EXCHANGE (default 1): 1 = sharded decode merges over the
+ * peer exchange when gla_comm_init could set it up, 0 = always the NCCL
+ * all-gather.  Set it to the same value on every rank (before
+ * gla_comm_init to skip the mapping). */
 int32_t gla_set_option(gla_ctx* ctx, int32_t option, int32_t value);
 
 /* ------------------------------------------------------------------------ */
@@ -256,13 +261,26 @@ int32_t gla_comm_unique_id_size(void);
 /* Writes a fresh unique id (rank 0 creates it and shares it out of band). */
 int32_t gla_comm_get_unique_id(void* unique_id);
 
-/* Joins an NCCL communicator of `nranks` ranks, one per GPU. */
+/* Joins an NCCL communicator of `nranks` ranks, one per GPU.  Collective.
+ * With GLA_OPT_SHARD_EXCHANGE on (the default) it also maps every rank's
+ * peer exchange buffer into every rank (CUDA IPC; the NCCL communicator
+ * carries the handles); the exchange is used only if every rank succeeded. */
 int32_t gla_comm_init(gla_ctx* ctx, int32_t nranks, int32_t rank, const void* unique_id);
 
+/* 1 if sharded decode on this context runs the peer exchange, 0 if it uses
+ * the NCCL all-gather.  No reference counterpart (introspection). */
+int32_t gla_comm_peer_exchange(const gla_ctx* ctx);
+
 /* Decode of one sequence whose KV rows are sharded across the communicator's
- * ranks (this rank holds n_pos_local rows).  Every rank computes its partial
- * record set, all-gathers the sets over NCCL and merges them: every rank ends
- * with the full xb.  Needs gla_comm_init first. */
+ * ranks (this rank holds n_pos_local >= 0 rows).  Every rank ends with the
+ * full xb.  Peer exchange (gla_comm_peer_exchange() == 1): one kernel
+ * computes the shard's per-head records, stores them into every rank's
+ * exchange buffer over NVLink, raises a flag per (rank, kv head) and merges
+ * all ranks' records as they arrive (bounded waits: a rank that does not
+ * take part within 1 s latches GLA_ERR_TIMEOUT).  Otherwise: partial record
+ * kernel, NCCL all-gather, merge kernel.  Every rank must make the same
+ * sequence of calls with the same shapes; capturable in a CUDA graph on the
+ * peer path.  Needs gla_comm_init first. */
 int32_t gla_decode_sharded_f16kv(gla_ctx* ctx, const float* q, const uint16_t* k,
                                  const uint16_t* v, float* xb, int32_t n_heads,
                                  int32_t n_kv_heads, int32_t head_dim, int64_t kv_stride,

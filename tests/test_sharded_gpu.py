@@ -1,7 +1,9 @@
-"""KV-sequence-sharded decode over NCCL (gla_decode_sharded_*), one process
-per GPU.  Needs >= 2 GPUs; skipped otherwise (the shard/merge math itself is
-covered on one GPU by test_decode_gpu.py::test_partial_records_and_combine and
-on CPU by test_multirank_host.py)."""
+"""KV-sequence-sharded decode (gla_decode_sharded_*), one process per GPU:
+the peer exchange (records stored into every rank's buffer over NVLink and
+merged inside the decode kernel) and the NCCL all-gather path.  Needs >= 2
+GPUs; skipped otherwise (the shard/merge math itself is covered on one GPU by
+test_decode_gpu.py::test_partial_records_and_combine and on CPU by
+test_multirank_host.py)."""
 import os
 import socket
 
@@ -11,6 +13,10 @@ import pytest
 import inputs
 
 pytestmark = pytest.mark.gpu
+
+NH, NKV, HD, T = 28, 4, 128, 20000
+N_CALLS = 4  # consecutive calls: both exchange parities, epochs advancing
+SCALES = [1.0 + 0.25 * i for i in range(N_CALLS)]  # q of call i = q * SCALES[i]
 
 
 def _n_gpus():
@@ -28,7 +34,15 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, f16, out_dir):
+def _shard(x, lo, hi, f16):
+    import torch
+
+    if f16:
+        return torch.from_numpy(inputs.to_f16_bits(x[lo:hi]).view(np.int16)).cuda()
+    return torch.from_numpy(np.ascontiguousarray(x[lo:hi])).cuda()
+
+
+def _rank_main(rank, world, port, f16, mode, out_dir):
     import datetime
 
     import torch
@@ -45,33 +59,40 @@ def _rank_main(rank, world, port, f16, out_dir):
                             timeout=datetime.timedelta(seconds=60))
     try:
         ctx = gla.Context(rank, torch.cuda.current_stream().cuda_stream)
+        if mode == "nccl":
+            ctx.set_option(gla.OPT_SHARD_EXCHANGE, 0)
         uid = [gla.Context.comm_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         ctx.comm_init(world, rank, uid[0])
-        nh, nkv, hd, T = 28, 4, 128, 20000
-        q, k, v = inputs.decode_case(91, nh, nkv, hd, T)
+        np.save(os.path.join(out_dir, f"peer{rank}.npy"), np.array([int(ctx.peer_exchange)]))
+        q, k, v = inputs.decode_case(91, NH, NKV, HD, T)
         lo, hi = sharding.kv_shard_bounds(T, world, rank)
-        if f16:
-            kk = inputs.to_f16_bits(k[lo:hi]).view(np.int16)
-            vv = inputs.to_f16_bits(v[lo:hi]).view(np.int16)
-        else:
-            kk, vv = np.ascontiguousarray(k[lo:hi]), np.ascontiguousarray(v[lo:hi])
-        qd = torch.from_numpy(q).cuda()
-        kd, vd = torch.from_numpy(kk).cuda(), torch.from_numpy(vv).cuda()
-        xb = torch.empty(nh * hd, device="cuda")
-        for _ in range(2):  # twice: the record buffers are reused
-            ctx.decode_sharded(qd, kd, vd, xb, nh, nkv, hd, hi - lo, f16_cache=f16)
+        kd, vd = _shard(k, lo, hi, f16), _shard(v, lo, hi, f16)
+        outs = []
+        for i in range(N_CALLS):  # back to back on the stream, read at the end
+            qd = torch.from_numpy(q * np.float32(SCALES[i])).cuda()
+            xb = torch.empty(NH * HD, device="cuda")
+            ctx.decode_sharded(qd, kd, vd, xb, NH, NKV, HD, hi - lo, f16_cache=f16)
+            outs.append(xb)
+        # one row in all: every other rank holds an empty shard
+        lo1, hi1 = sharding.kv_shard_bounds(1, world, rank)
+        k1, v1 = _shard(k, 0, 1, f16), _shard(v, 0, 1, f16)
+        xb1 = torch.empty(NH * HD, device="cuda")
+        ctx.decode_sharded(torch.from_numpy(q).cuda(), k1, v1, xb1, NH, NKV, HD, hi1 - lo1,
+                           f16_cache=f16)
         torch.cuda.synchronize()
         assert ctx.device_status() == 0
-        np.save(os.path.join(out_dir, f"xb{rank}.npy"), xb.cpu().numpy())
+        np.save(os.path.join(out_dir, f"xb{rank}.npy"), torch.stack(outs).cpu().numpy())
+        np.save(os.path.join(out_dir, f"one{rank}.npy"), xb1.cpu().numpy())
         dist.barrier()
         ctx.close()
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("mode", ["peer", "nccl"])
 @pytest.mark.parametrize("f16", [True, False], ids=["f16kv", "f32kv"])
-def test_sharded_decode_two_gpus(tmp_path, oracle, f16):
+def test_sharded_decode_two_gpus(tmp_path, oracle, f16, mode):
     if _n_gpus() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -79,22 +100,28 @@ def test_sharded_decode_two_gpus(tmp_path, oracle, f16):
     world = 2
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, f16, str(tmp_path)))
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, f16, mode, str(tmp_path)))
              for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=300)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    nh, nkv, hd, T = 28, 4, 128, 20000
-    q, k, v = inputs.decode_case(91, nh, nkv, hd, T)
-    if f16:
-        ref = oracle.decode_f16(q, inputs.to_f16_bits(k), inputs.to_f16_bits(v), nh, nkv, hd, T)
-        tol = 5e-3
-    else:
-        ref = oracle.decode_f32(q, k, v, nh, nkv, hd, T)
-        tol = 1e-3
+    for r in range(world):
+        used_peer = bool(np.load(tmp_path / f"peer{r}.npy")[0])
+        assert used_peer == (mode == "peer"), (r, used_peer)
+    q, k, v = inputs.decode_case(91, NH, NKV, HD, T)
+    tol = 5e-3 if f16 else 1e-3
+    kk = inputs.to_f16_bits(k) if f16 else k
+    vv = inputs.to_f16_bits(v) if f16 else v
+    dec = oracle.decode_f16 if f16 else oracle.decode_f32
+    refs = [dec(q * np.float32(s), kk, vv, NH, NKV, HD, T) for s in SCALES]
+    ref1 = dec(q, kk, vv, NH, NKV, HD, 1)
     for r in range(world):
         got = np.load(tmp_path / f"xb{r}.npy")
-        err = np.abs(got - ref).max()
-        assert err <= tol and err / np.abs(ref).max() <= tol, (r, err)
+        for i, ref in enumerate(refs):
+            err = np.abs(got[i] - ref).max()
+            assert err <= tol and err / np.abs(ref).max() <= tol, (r, i, err)
+        one = np.load(tmp_path / f"one{r}.npy")
+        err = np.abs(one - ref1).max()
+        assert err <= tol and err / np.abs(ref1).max() <= tol, (r, "one row", err)
