@@ -262,7 +262,8 @@ int sharded(gla_ctx* ctx, int dtype, const float* q, const void* k, const void* 
     ctx->records_cap = rec;
   }
   int rc;
-  if (ctx->opt_shard_exchange && ctx->xch.active() && rec <= (size_t)gla::kXchRecFloats &&
+  if (ctx->opt_shard_exchange && ctx->xch.active() &&
+      (size_t)n_heads * (head_dim + 4) <= (size_t)gla::kXchRecFloats &&
       n_kv_heads <= gla::kXchMaxSeg) {
     // one kernel: shard attention, records to every rank over peer memory,
     // merge; an empty shard (n_pos_local == 0) still publishes empty records

@@ -536,11 +536,26 @@ struct F16Consumer {
 // ---------------------------------------------------------------------------
 // Output helpers
 // ---------------------------------------------------------------------------
+// Exchange-buffer record row: o[HD], m, l, 2 pad (16-byte rows).
+template <int HD>
+constexpr int xch_row_floats() { return HD + 4; }
+
+// record_mode 2 writes this rank's record straight into slot [par][own rank]
+// of every rank's exchange buffer (peer stores over NVLink).
 template <int HD>
 __device__ __forceinline__ void write_final(const DecodeArgs& a, int b, int hq, int d, float O,
-                                            float M, float L) {
+                                            float M, float L, int par = 0) {
   const int64_t row = (int64_t)b * a.n_heads + hq;
-  if (a.record_mode) {
+  if (a.record_mode == 2) {
+    const float o = L > 0.f ? O / L : 0.f;
+    const float m = L > 0.f ? M * kLn2 : -INFINITY;
+    for (int r = 0; r < a.xch_world; ++r) {
+      float* rec = reinterpret_cast<float*>(a.xch_bases[r] + xch_rec_offset(par, a.xch_rank)) +
+                   row * xch_row_floats<HD>();
+      rec[d] = o;
+      if (d == 0) *reinterpret_cast<float2*>(rec + HD) = make_float2(m, L);
+    }
+  } else if (a.record_mode) {
     float* rec = a.out + row * (HD + 2);
     rec[d] = L > 0.f ? O / L : 0.f;
     if (d == 0) {
@@ -554,8 +569,22 @@ __device__ __forceinline__ void write_final(const DecodeArgs& a, int b, int hq, 
 
 template <int HD>
 __device__ __forceinline__ void write_final4(const DecodeArgs& a, int b, int hq, int d, float4 O,
-                                             float M, float L) {
-  if (a.record_mode) {
+                                             float M, float L, int par = 0) {
+  if (a.record_mode == 2) {
+    float4 o;
+    o.x = L > 0.f ? O.x / L : 0.f;
+    o.y = L > 0.f ? O.y / L : 0.f;
+    o.z = L > 0.f ? O.z / L : 0.f;
+    o.w = L > 0.f ? O.w / L : 0.f;
+    const float m = L > 0.f ? M * kLn2 : -INFINITY;
+    const int64_t row = (int64_t)b * a.n_heads + hq;
+    for (int r = 0; r < a.xch_world; ++r) {
+      float* rec = reinterpret_cast<float*>(a.xch_bases[r] + xch_rec_offset(par, a.xch_rank)) +
+                   row * xch_row_floats<HD>();
+      *reinterpret_cast<float4*>(rec + d) = o;
+      if (d == 0) *reinterpret_cast<float2*>(rec + HD) = make_float2(m, L);
+    }
+  } else if (a.record_mode) {
     write_final<HD>(a, b, hq, d, O.x, M, L);
     write_final<HD>(a, b, hq, d + 1, O.y, M, L);
     write_final<HD>(a, b, hq, d + 2, O.z, M, L);
@@ -597,7 +626,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   int32_t* npos = nunits + B;                                         // [B]
   float* qs = reinterpret_cast<float*>(smem + a.off_q);                // [kMaxGroup][HD]
   float* pbuf = reinterpret_cast<float*>(smem + a.off_pbuf);           // [NW][kPbufFloats]
-  float* merge = reinterpret_cast<float*>(smem + a.off_merge);         // [NW][kMG][HD+2]
+  float* merge = reinterpret_cast<float*>(smem + a.off_merge);         // [NW][kMG][HD+4]
   volatile int* flags = reinterpret_cast<volatile int*>(smem + a.off_flags);  // [0]=abort [1]=last
 
   if (tid == 0) {
@@ -699,10 +728,6 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   pdl_wait();
   pdl_launch_dependents();
   if (!early) scan_sequences();
-  // peer exchange: this call's epoch (calls completed on this rank + 1), read
-  // once per CTA after the wait (the previous call's last CTA advances it)
-  if (a.record_mode == 2 && tid == 0)
-    flags[2] = (int)(*reinterpret_cast<volatile uint32_t*>(a.xch_local + xch_epoch_offset()) + 1u);
   __syncthreads();
 
   const int32_t W = seq_start[B];
@@ -772,30 +797,30 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   }
 
   // ---------------- consumers ----------------
-  // Peer exchange (record_mode 2, one sequence): the finished records of kv
-  // head g (written to a.out by this CTA's threads) go to slot [parity][own
-  // rank] of every rank's exchange buffer with plain peer stores; after a
-  // system fence one thread raises flag [parity][own rank][g] on every rank.
-  // Then every rank's flag for g is awaited in this rank's buffer (bounded:
-  // a missing rank latches GLA_ERR_TIMEOUT) and the world records of g are
-  // merged into xb: M = max m_r, w_r = l_r e^(m_r - M),
-  // xb = sum w_r o_r / sum w_r.
+  // Peer exchange (record_mode 2, one sequence).  The CTA that holds kv head
+  // g's final records reads g's epoch first (epoch_read; parity = epoch & 1)
+  // and write_final stores the records straight into slot [parity][own rank]
+  // of every rank's exchange buffer.  publish_merge then raises flag
+  // [parity][own rank][g] on every rank (release at system scope after the
+  // CTA barrier), advances g's epoch, waits for every rank's flag for g in
+  // this rank's buffer (bounded: a missing rank latches GLA_ERR_TIMEOUT) and
+  // merges the world records into xb: M = max m_r, w_r = l_r e^(m_r - M),
+  // xb = sum w_r o_r / sum w_r.  Only the publishing CTA reads or advances
+  // g's epoch, after the dependency wait, so the previous call's advance is
+  // visible.
+  auto epoch_read = [&](int g) {
+    if (a.record_mode == 2 && tid == 0)
+      flags[2] = (int)(*reinterpret_cast<volatile uint32_t*>(a.xch_local + xch_epoch_offset(g)) + 1u);
+  };
   auto publish_merge = [&](int g) {
+    consumer_sync(kNCT);  // every record store of this CTA precedes the flags
     const uint32_t ep = (uint32_t)flags[2];
     const int par = (int)(ep & 1u), W = a.xch_world, me = a.xch_rank;
-    const int nf = G * (HD + 2);
-    const float* src = a.out + (int64_t)g * G * (HD + 2);
-    for (int r = 0; r < W; ++r) {
-      float* dst = reinterpret_cast<float*>(a.xch_bases[r] + xch_rec_offset(par, me)) +
-                   (int64_t)g * G * (HD + 2);
-      for (int i = tid; i < nf; i += kNCT) dst[i] = src[i];
-    }
-    consumer_sync(kNCT);
     if (tid == 0) {
-      __threadfence_system();
       for (int r = 0; r < W; ++r)
-        st_relaxed_sys_u32(reinterpret_cast<uint32_t*>(a.xch_bases[r] + xch_flag_offset(par, me, g)),
+        st_release_sys_u32(reinterpret_cast<uint32_t*>(a.xch_bases[r] + xch_flag_offset(par, me, g)),
                            ep);
+      *reinterpret_cast<volatile uint32_t*>(a.xch_local + xch_epoch_offset(g)) = ep;
     }
     if (tid < W) {
       const uint32_t* f = reinterpret_cast<const uint32_t*>(a.xch_local + xch_flag_offset(par, tid, g));
@@ -812,61 +837,60 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
       }
     }
     consumer_sync(kNCT);
-    for (int idx = tid; idx < G * HD; idx += kNCT) {
-      const int hq = g * G + idx / HD, d = idx % HD;
-      float M = -INFINITY;
-      for (int r = 0; r < W; ++r) {
-        const float* rec = reinterpret_cast<const float*>(a.xch_local + xch_rec_offset(par, r)) +
-                           (int64_t)hq * (HD + 2);
-        if (ld_cg(rec + HD + 1) > 0.f) M = fmaxf(M, ld_cg(rec + HD));
-      }
-      float O = 0.f, L = 0.f;
-      if (M != -INFINITY) {
-        for (int r = 0; r < W; ++r) {
+    // one thread per (head, 4 columns); all of its loads in flight at once
+    constexpr int kXR = xch_row_floats<HD>();
+    constexpr int kD4 = HD / 4;
+    for (int it = tid; it < G * kD4; it += kNCT) {
+      const int hq = g * G + it / kD4, d = (it % kD4) * 4;
+      float2 ml[kXchMaxWorld];
+      float4 o[kXchMaxWorld];
+#pragma unroll
+      for (int r = 0; r < kXchMaxWorld; ++r) {
+        if (r < W) {
           const float* rec = reinterpret_cast<const float*>(a.xch_local + xch_rec_offset(par, r)) +
-                             (int64_t)hq * (HD + 2);
-          const float l = ld_cg(rec + HD + 1);
-          if (l > 0.f) {
-            const float w = l * __expf(ld_cg(rec + HD) - M);
-            O += w * ld_cg(rec + d);
+                             (int64_t)hq * kXR;
+          ml[r] = __ldcg(reinterpret_cast<const float2*>(rec + HD));
+          o[r] = __ldcg(reinterpret_cast<const float4*>(rec + d));
+        } else {
+          ml[r] = make_float2(-INFINITY, 0.f);
+          o[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      float M = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < kXchMaxWorld; ++r)
+        if (ml[r].y > 0.f) M = fmaxf(M, ml[r].x);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      float L = 0.f;
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int r = 0; r < kXchMaxWorld; ++r) {
+          if (ml[r].y > 0.f) {
+            const float w = ml[r].y * __expf(ml[r].x - M);
+            acc.x += w * o[r].x; acc.y += w * o[r].y; acc.z += w * o[r].z; acc.w += w * o[r].w;
             L += w;
           }
         }
       }
-      a.xch_out[(int64_t)hq * HD + d] = L > 0.f ? O / L : 0.f;
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      *reinterpret_cast<float4*>(a.xch_out + (int64_t)hq * HD + d) =
+          make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
     }
     consumer_sync(kNCT);
-  };
-  // Peer exchange: the last CTA of the call to finish advances the epoch.
-  auto cta_exit = [&]() {
-    if (a.record_mode != 2) return;
-    consumer_sync(kNCT);
-    if (tid == 0) {
-      int32_t* done = reinterpret_cast<int32_t*>(a.xch_local + xch_done_offset());
-      if (atomic_add_acq_rel_gpu(done, 1) == (int)gridDim.x - 1) {
-        *reinterpret_cast<volatile int32_t*>(done) = 0;
-        *reinterpret_cast<volatile uint32_t*>(a.xch_local + xch_epoch_offset()) =
-            (uint32_t)flags[2];
-      }
-    }
   };
 
   // segments with no rows (n_pos <= 0) produce zeros / empty records
   for (int s = blockIdx.x; s < B * n_kv; s += gridDim.x) {
     const int b = s / n_kv, g = s - b * n_kv;
     if (nunits[b] == 0) {
+      epoch_read(g);
+      consumer_sync(kNCT);
       for (int idx = tid; idx < G * HD; idx += kNCT)
-        write_final<HD>(a, b, g * G + idx / HD, idx % HD, 0.f, 0.f, 0.f);
-      if (a.record_mode == 2) {
-        consumer_sync(kNCT);
-        publish_merge(g);
-      }
+        write_final<HD>(a, b, g * G + idx / HD, idx % HD, 0.f, 0.f, 0.f, flags[2] & 1);
+      if (a.record_mode == 2) publish_merge(g);
     }
   }
-  if (my_count == 0) {
-    cta_exit();
-    return;
-  }
+  if (my_count == 0) return;
 
   Consumer cons;
   float* pbuf_w = pbuf + warp * Consumer::kPbufFloats;
@@ -946,7 +970,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
         L = L * sa + Lo * sb;
         M = Mn;
       }
-      if (active && j == 0) write_final4<HD>(a, b, g * G + h, d, O, M, L);
+      if (active && j == 0) write_final4<HD>(a, b, g * G + h, d, O, M, L, flags[2] & 1);
     }
   };
 
@@ -980,7 +1004,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
         }
       }
       if (npieces == 1) {
-        write_final4<HD>(a, b, g * G + h, d, O, M, L);
+        write_final4<HD>(a, b, g * G + h, d, O, M, L, flags[2] & 1);
       } else {
         float* slot = a.ws_part + ((int64_t)(blockIdx.x + s) * G + h) * kSH;
         *reinterpret_cast<float4*>(slot + d) = O;
@@ -1013,6 +1037,9 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   int st = 0;
   uint32_t phase = 0;
   while (wk.next_piece(nunits, B, n_kv, pc)) {
+    // kv head pc.g's exchange epoch (read by every CTA holding a piece of it,
+    // advanced only by its publisher), loaded alongside q
+    epoch_read(pc.g);
     load_q(pc.b, pc.g);
     cons.begin(a, qs, lane);
     const int np = npos[pc.b];
@@ -1030,7 +1057,6 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
     }
     finish_piece(pc.b, pc.g);
   }
-  cta_exit();
 }
 
 }  // namespace gla

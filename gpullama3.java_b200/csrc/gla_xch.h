@@ -2,8 +2,8 @@
 // decode (one per rank, mapped into every other rank with CUDA IPC).
 //
 // Each rank publishes its shard's per-head records (o normalised, m in
-// natural-log units, l; [n_heads][head_dim + 2] floats, the layout of
-// gla_decode_partial_*) into slot [parity][own rank] of EVERY rank's buffer
+// natural-log units, l, 2 pad: [n_heads][head_dim + 4] floats, 16-byte rows)
+// into slot [parity][own rank] of EVERY rank's buffer
 // with plain peer stores, then raises flag [parity][own rank][kv head] on
 // every rank.  A rank merges kv head g once the flags of all ranks for g
 // carry the call's epoch.  Two parities: a rank can run at most one call
@@ -12,8 +12,8 @@
 //
 //   records  [2][kXchMaxWorld][kXchRecFloats]   float
 //   flags    [2][kXchMaxWorld][kXchMaxSeg]      uint32 (epoch of the write)
-//   epoch    uint32: calls completed on this rank (advanced by the last CTA)
-//   done     int32 : CTAs of the running call that have finished
+//   epochs   [kXchMaxSeg] uint32: calls completed for kv head g on this rank,
+//            read and advanced only by the CTA that publishes g (one per call)
 #pragma once
 
 #include <stddef.h>
@@ -28,7 +28,7 @@
 namespace gla {
 
 constexpr int kXchMaxWorld = 8;
-constexpr int kXchRecFloats = 128 * (128 + 2);  // up to 128 heads of head_dim 128
+constexpr int kXchRecFloats = 128 * (128 + 4);  // up to 128 heads of head_dim 128
 constexpr int kXchMaxSeg = 128;                 // kv heads of one call
 
 GLA_XCH_HD size_t xch_rec_offset(int parity, int src) {  // bytes
@@ -40,10 +40,9 @@ GLA_XCH_HD size_t xch_flags_base() {
 GLA_XCH_HD size_t xch_flag_offset(int parity, int src, int seg) {
   return xch_flags_base() + (((size_t)parity * kXchMaxWorld + src) * kXchMaxSeg + seg) * 4;
 }
-GLA_XCH_HD size_t xch_epoch_offset() {
-  return xch_flags_base() + (size_t)2 * kXchMaxWorld * kXchMaxSeg * 4;
+GLA_XCH_HD size_t xch_epoch_offset(int seg) {
+  return xch_flags_base() + (size_t)2 * kXchMaxWorld * kXchMaxSeg * 4 + (size_t)seg * 4;
 }
-GLA_XCH_HD size_t xch_done_offset() { return xch_epoch_offset() + 128; }
-GLA_XCH_HD size_t xch_bytes() { return xch_epoch_offset() + 256; }
+GLA_XCH_HD size_t xch_bytes() { return xch_epoch_offset(kXchMaxSeg); }
 
 }  // namespace gla
