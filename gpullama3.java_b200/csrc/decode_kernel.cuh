@@ -7,27 +7,32 @@
 // workgroup per q head).
 //
 // Structure (one persistent CTA per SM):
-//  * The tiles of all (sequence, kv head) segments are dealt to the CTAs in
-//    contiguous near-equal ranges (gla_common.cuh), so every SM streams the
-//    same number of KV bytes whatever the sequence lengths.
+//  * The 64-row tiles of all (sequence, kv head) segments are dealt to the
+//    CTAs (gla_common.cuh, Deal): one sequence gives each kv head its own
+//    group of CTAs; batches are dealt in contiguous near-equal ranges, so
+//    every SM streams the same number of KV bytes whatever the lengths.
 //  * Warp NW is the producer.  It fills a ring of `stages` shared-memory
 //    stages guarded by full/empty mbarriers, one K tile and one V tile
 //    (`tile` rows of one kv head) per stage:
 //      LOADER 0 (single sequence): tiled TMA, one cp.async.bulk.tensor.2d per
 //        tensor and column block through a 2D tensor map [rows][kv_stride];
-//        FP16 tiles land 128B/64B-swizzled so ldmatrix is conflict-free;
-//        rows past the cache end are zero-filled by the TMA unit.
+//        tiles land 128B/64B-swizzled so shared-memory reads are
+//        conflict-free; rows past the cache end are zero-filled by the TMA
+//        unit.  The first ring pass of cache history may be fetched before
+//        the dependency wait (early prefetch, see the kernel).
 //      LOADER 1 (batched, per-sequence pointers read on the device): 16-byte
 //        cp.async into the same swizzled layout, completion via
 //        cp.async.mbarrier.arrive.
-//  * Warps 0..NW-1 consume every stage together; each owns 16 rows of the
-//    tile and keeps its own online-softmax state (m, l, o) for all G q heads
-//    of the group, so all heads of a group share one K/V tile read and no
-//    CTA-wide barrier is needed per tile.
+//  * Warps 0..NW-1 consume every stage together; each owns a fixed slice of
+//    the tile's rows and keeps its own online-softmax state (m, l, o) for all
+//    G q heads of the group, so all heads of a group share one K/V tile read
+//    and no CTA-wide barrier is needed per tile.
 //  * At the end of a segment piece the warps merge their states in shared
 //    memory.  A segment held by one CTA is written straight to xb; otherwise
 //    each CTA stores its piece to a workspace slot and the last CTA to finish
 //    (atomic counter, reset by that CTA) merges the pieces (log-sum-exp).
+//    Sharded sequences (record mode 2) then exchange per-rank records over
+//    peer memory and merge them in the same kernel (publish_merge).
 //
 // Consumers: F32Consumer (FP32 cache, CUDA-core FMA: the FP32 cache delivers
 // at most G/2 FLOP per byte) and F16Consumer (FP16 cache, mma.sync m16n8k16
