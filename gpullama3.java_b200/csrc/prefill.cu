@@ -389,14 +389,16 @@ __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
         for (int t = 0; t < NT; ++t) {
           const int nb_t = qb * NT + t + 1;
           if (j >= nb_t) continue;
-          ok = ok && mbar_wait(&p_full[t], (uint32_t)(j & 1), abort_flag, a.status);
-          tc_fence_after();
-          issue_pv(t, j);
+          // S_t(j+1) first: the tile's next softmax waits on it, while
+          // P_t(j) V_j is needed only before P_t(j+1) is written
           if (j + 1 < nb_t) {
             ok = ok && mbar_wait(&s_empty[t], (uint32_t)(j & 1), abort_flag, a.status);
             tc_fence_after();
             issue_s(t, j + 1);
           }
+          ok = ok && mbar_wait(&p_full[t], (uint32_t)(j & 1), abort_flag, a.status);
+          tc_fence_after();
+          issue_pv(t, j);
         }
         tc_commit(&v_empty[j % VS]);
         if (next_k) tc_commit(&k_empty[(j + 1) % KS]);
