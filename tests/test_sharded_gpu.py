@@ -90,14 +90,9 @@ def _rank_main(rank, world, port, f16, mode, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["peer", "nccl"])
-@pytest.mark.parametrize("f16", [True, False], ids=["f16kv", "f32kv"])
-def test_sharded_decode_two_gpus(tmp_path, oracle, f16, mode):
-    if _n_gpus() < 2:
-        pytest.skip("needs 2 GPUs")
+def _run_world(tmp_path, oracle, f16, mode, world):
     import torch.multiprocessing as mp
 
-    world = 2
     ctx = mp.get_context("spawn")
     port = _free_port()
     procs = [ctx.Process(target=_rank_main, args=(r, world, port, f16, mode, str(tmp_path)))
@@ -125,3 +120,18 @@ def test_sharded_decode_two_gpus(tmp_path, oracle, f16, mode):
         one = np.load(tmp_path / f"one{r}.npy")
         err = np.abs(one - ref1).max()
         assert err <= tol and err / np.abs(ref1).max() <= tol, (r, "one row", err)
+
+
+@pytest.mark.parametrize("mode", ["peer", "nccl"])
+@pytest.mark.parametrize("f16", [True, False], ids=["f16kv", "f32kv"])
+def test_sharded_decode_two_gpus(tmp_path, oracle, f16, mode):
+    if _n_gpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    _run_world(tmp_path, oracle, f16, mode, 2)
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_sharded_decode_peer_exchange_wider(tmp_path, oracle, world):
+    if _n_gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    _run_world(tmp_path, oracle, True, "peer", world)
