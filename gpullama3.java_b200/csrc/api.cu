@@ -263,7 +263,7 @@ int sharded(gla_ctx* ctx, int dtype, const float* q, const void* k, const void* 
   }
   int rc;
   if (ctx->opt_shard_exchange && ctx->xch.active() &&
-      (size_t)n_heads * (head_dim + 4) <= (size_t)gla::kXchRecFloats &&
+      (size_t)n_heads * (head_dim + 4) <= (size_t)gla::kXchRecWords &&
       n_kv_heads <= gla::kXchMaxSeg) {
     // one kernel: shard attention, records to every rank over peer memory,
     // merge; an empty shard (n_pos_local == 0) still publishes empty records

@@ -81,9 +81,9 @@ void ensure_smem_attr(Kern kern, size_t bytes, std::atomic<uint64_t>& done) {
     done.fetch_or(bit, std::memory_order_acq_rel);
 }
 
-template <int HD, class C, int LOADER>
+template <int HD, class C, int LOADER, bool XCH>
 cudaError_t launch_impl(const DecodeArgs& a, const DecodePlan& p, cudaStream_t st) {
-  auto kern = decode_kernel<HD, C, LOADER>;
+  auto kern = decode_kernel<HD, C, LOADER, XCH>;
   static std::atomic<uint64_t> smem_set{0};  // one per kernel instantiation
   ensure_smem_attr(kern, p.smem, smem_set);
   // programmatic dependent launch: this grid's CTAs may start (prologue
@@ -102,31 +102,31 @@ cudaError_t launch_impl(const DecodeArgs& a, const DecodePlan& p, cudaStream_t s
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
-template <int HD, int LOADER>
+template <int HD, int LOADER, bool XCH>
 cudaError_t launch_f32(const DecodeArgs& a, const DecodePlan& p, cudaStream_t st) {
   switch (group_cap_for(GLA_DTYPE_F32, a.group)) {
-    case 1: return launch_impl<HD, F32Consumer<HD, 1>, LOADER>(a, p, st);
-    case 2: return launch_impl<HD, F32Consumer<HD, 2>, LOADER>(a, p, st);
-    case 3: return launch_impl<HD, F32Consumer<HD, 3>, LOADER>(a, p, st);
-    case 4: return launch_impl<HD, F32Consumer<HD, 4>, LOADER>(a, p, st);
-    default: return launch_impl<HD, F32Consumer<HD, 8>, LOADER>(a, p, st);
+    case 1: return launch_impl<HD, F32Consumer<HD, 1>, LOADER, XCH>(a, p, st);
+    case 2: return launch_impl<HD, F32Consumer<HD, 2>, LOADER, XCH>(a, p, st);
+    case 3: return launch_impl<HD, F32Consumer<HD, 3>, LOADER, XCH>(a, p, st);
+    case 4: return launch_impl<HD, F32Consumer<HD, 4>, LOADER, XCH>(a, p, st);
+    default: return launch_impl<HD, F32Consumer<HD, 8>, LOADER, XCH>(a, p, st);
   }
 }
 
-template <int LOADER>
+template <int LOADER, bool XCH>
 cudaError_t launch_any(int dtype, int hd, const DecodeArgs& a, const DecodePlan& p,
                        cudaStream_t st) {
   if (dtype == GLA_DTYPE_F32) {
     switch (hd) {
-      case 64: return launch_f32<64, LOADER>(a, p, st);
-      case 96: return launch_f32<96, LOADER>(a, p, st);
-      default: return launch_f32<128, LOADER>(a, p, st);
+      case 64: return launch_f32<64, LOADER, XCH>(a, p, st);
+      case 96: return launch_f32<96, LOADER, XCH>(a, p, st);
+      default: return launch_f32<128, LOADER, XCH>(a, p, st);
     }
   }
   switch (hd) {
-    case 64: return launch_impl<64, F16Consumer<64>, LOADER>(a, p, st);
-    case 96: return launch_impl<96, F16Consumer<96>, LOADER>(a, p, st);
-    default: return launch_impl<128, F16Consumer<128>, LOADER>(a, p, st);
+    case 64: return launch_impl<64, F16Consumer<64>, LOADER, XCH>(a, p, st);
+    case 96: return launch_impl<96, F16Consumer<96>, LOADER, XCH>(a, p, st);
+    default: return launch_impl<128, F16Consumer<128>, LOADER, XCH>(a, p, st);
   }
 }
 
@@ -275,8 +275,11 @@ int launch_decode(const DecodeRequest& r, const DecodePlan& p, float* ws_part, i
   a.off_q = L.off_q;
   a.off_merge = L.off_merge;
   a.off_flags = L.off_flags;
-  cudaError_t rc = loader == 0 ? launch_any<0>(r.dtype, hd, a, p, stream)
-                                : launch_any<1>(r.dtype, hd, a, p, stream);
+  // the peer exchange (record mode 2: one sequence, tensor-map loader) is a
+  // separate instantiation, so the other kernels carry none of its registers
+  cudaError_t rc = r.record_mode == 2 && loader == 0 ? launch_any<0, true>(r.dtype, hd, a, p, stream)
+                   : loader == 0                     ? launch_any<0, false>(r.dtype, hd, a, p, stream)
+                                                     : launch_any<1, false>(r.dtype, hd, a, p, stream);
   if (rc != cudaSuccess) {
     *err = std::string("decode launch failed: ") + cudaGetErrorString(rc);
     return GLA_ERR_CUDA;

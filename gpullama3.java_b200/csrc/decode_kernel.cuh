@@ -545,20 +545,31 @@ struct F16Consumer {
 template <int HD>
 constexpr int xch_row_floats() { return HD + 4; }
 
-// record_mode 2 writes this rank's record straight into slot [par][own rank]
-// of every rank's exchange buffer (peer stores over NVLink).
-template <int HD>
+// An exchange word: the value's bits and the call's epoch, stored and loaded
+// as one 64-bit single-copy-atomic access.
+__device__ __forceinline__ uint64_t xch_word(float v, uint32_t ep) {
+  return (uint64_t)__float_as_uint(v) | ((uint64_t)ep << 32);
+}
+
+// record_mode 2 writes this rank's record straight into slot [ep & 1][own
+// rank] of every rank's exchange buffer (peer stores over NVLink), each word
+// tagged with the call's epoch `ep`.
+template <int HD, bool XCH = false>
 __device__ __forceinline__ void write_final(const DecodeArgs& a, int b, int hq, int d, float O,
-                                            float M, float L, int par = 0) {
+                                            float M, float L, uint32_t ep = 0) {
   const int64_t row = (int64_t)b * a.n_heads + hq;
-  if (a.record_mode == 2) {
+  if constexpr (XCH) {
     const float o = L > 0.f ? O / L : 0.f;
     const float m = L > 0.f ? M * kLn2 : -INFINITY;
     for (int r = 0; r < a.xch_world; ++r) {
-      float* rec = reinterpret_cast<float*>(a.xch_bases[r] + xch_rec_offset(par, a.xch_rank)) +
-                   row * xch_row_floats<HD>();
-      rec[d] = o;
-      if (d == 0) *reinterpret_cast<float2*>(rec + HD) = make_float2(m, L);
+      uint64_t* rec =
+          reinterpret_cast<uint64_t*>(a.xch_bases[r] + xch_rec_offset((int)(ep & 1u), a.xch_rank)) +
+          row * xch_row_floats<HD>();
+      st_relaxed_sys_u64(rec + d, xch_word(o, ep));
+      if (d == 0) {
+        st_relaxed_sys_u64(rec + HD, xch_word(m, ep));
+        st_relaxed_sys_u64(rec + HD + 1, xch_word(L, ep));
+      }
     }
   } else if (a.record_mode) {
     float* rec = a.out + row * (HD + 2);
@@ -572,22 +583,21 @@ __device__ __forceinline__ void write_final(const DecodeArgs& a, int b, int hq, 
   }
 }
 
-template <int HD>
+template <int HD, bool XCH = false>
 __device__ __forceinline__ void write_final4(const DecodeArgs& a, int b, int hq, int d, float4 O,
-                                             float M, float L, int par = 0) {
-  if (a.record_mode == 2) {
-    float4 o;
-    o.x = L > 0.f ? O.x / L : 0.f;
-    o.y = L > 0.f ? O.y / L : 0.f;
-    o.z = L > 0.f ? O.z / L : 0.f;
-    o.w = L > 0.f ? O.w / L : 0.f;
+                                             float M, float L, uint32_t ep = 0) {
+  if constexpr (XCH) {
     const float m = L > 0.f ? M * kLn2 : -INFINITY;
     const int64_t row = (int64_t)b * a.n_heads + hq;
+    const uint64_t w0 = xch_word(L > 0.f ? O.x / L : 0.f, ep), w1 = xch_word(L > 0.f ? O.y / L : 0.f, ep);
+    const uint64_t w2 = xch_word(L > 0.f ? O.z / L : 0.f, ep), w3 = xch_word(L > 0.f ? O.w / L : 0.f, ep);
     for (int r = 0; r < a.xch_world; ++r) {
-      float* rec = reinterpret_cast<float*>(a.xch_bases[r] + xch_rec_offset(par, a.xch_rank)) +
-                   row * xch_row_floats<HD>();
-      *reinterpret_cast<float4*>(rec + d) = o;
-      if (d == 0) *reinterpret_cast<float2*>(rec + HD) = make_float2(m, L);
+      uint64_t* rec =
+          reinterpret_cast<uint64_t*>(a.xch_bases[r] + xch_rec_offset((int)(ep & 1u), a.xch_rank)) +
+          row * xch_row_floats<HD>();
+      st_relaxed_sys_u64x2(rec + d, w0, w1);  // rows are 32-byte aligned, d % 4 == 0
+      st_relaxed_sys_u64x2(rec + d + 2, w2, w3);
+      if (d == 0) st_relaxed_sys_u64x2(rec + HD, xch_word(m, ep), xch_word(L, ep));
     }
   } else if (a.record_mode) {
     write_final<HD>(a, b, hq, d, O.x, M, L);
@@ -608,7 +618,7 @@ __device__ __forceinline__ void write_final4(const DecodeArgs& a, int b, int hq,
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
-template <int HD, class Consumer, int LOADER>
+template <int HD, class Consumer, int LOADER, bool XCH>
 __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
     decode_kernel(const __grid_constant__ DecodeArgs a) {
   extern __shared__ __align__(1024) char smem_raw[];
@@ -803,77 +813,74 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
 
   // ---------------- consumers ----------------
   // Peer exchange (record_mode 2, one sequence).  The CTA that holds kv head
-  // g's final records reads g's epoch first (epoch_read; parity = epoch & 1)
-  // and write_final stores the records straight into slot [parity][own rank]
-  // of every rank's exchange buffer.  publish_merge then raises flag
-  // [parity][own rank][g] on every rank (release at system scope after the
-  // CTA barrier), advances g's epoch, waits for every rank's flag for g in
-  // this rank's buffer (bounded: a missing rank latches GLA_ERR_TIMEOUT) and
-  // merges the world records into xb: M = max m_r, w_r = l_r e^(m_r - M),
-  // xb = sum w_r o_r / sum w_r.  Only the publishing CTA reads or advances
-  // g's epoch, after the dependency wait, so the previous call's advance is
-  // visible.
+  // g's final records reads g's epoch first (epoch_read) and write_final
+  // stores the records, each word tagged with the epoch, straight into slot
+  // [epoch & 1][own rank] of every rank's exchange buffer.  publish_merge
+  // advances g's epoch and merges the world records of g into xb as they
+  // arrive: every thread polls its words until all carry the call's epoch
+  // (bounded: a rank that never writes latches GLA_ERR_TIMEOUT), then
+  // M = max m_r, w_r = l_r e^(m_r - M), xb = sum w_r o_r / sum w_r.  Only the
+  // publishing CTA reads or advances g's epoch, after the dependency wait,
+  // so the previous call's advance is visible.
   auto epoch_read = [&](int g) {
-    if (a.record_mode == 2 && tid == 0)
+    if (XCH && tid == 0)
       flags[2] = (int)(*reinterpret_cast<volatile uint32_t*>(a.xch_local + xch_epoch_offset(g)) + 1u);
   };
   auto publish_merge = [&](int g) {
-    consumer_sync(kNCT);  // every record store of this CTA precedes the flags
+    if constexpr (!XCH) return;
     const uint32_t ep = (uint32_t)flags[2];
-    const int par = (int)(ep & 1u), W = a.xch_world, me = a.xch_rank;
-    if (tid == 0) {
-      for (int r = 0; r < W; ++r)
-        st_release_sys_u32(reinterpret_cast<uint32_t*>(a.xch_bases[r] + xch_flag_offset(par, me, g)),
-                           ep);
-      *reinterpret_cast<volatile uint32_t*>(a.xch_local + xch_epoch_offset(g)) = ep;
-    }
-    if (tid < W) {
-      const uint32_t* f = reinterpret_cast<const uint32_t*>(a.xch_local + xch_flag_offset(par, tid, g));
-      if (ld_acquire_sys_u32(f) != ep) {
-        const unsigned long long t0 = global_timer_ns();
-        while (ld_acquire_sys_u32(f) != ep) {
-          if (flags[0]) break;
-          if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+    const int par = (int)(ep & 1u), W = a.xch_world;
+    if (tid == 0) *reinterpret_cast<volatile uint32_t*>(a.xch_local + xch_epoch_offset(g)) = ep;
+    constexpr int kXR = xch_row_floats<HD>();
+    constexpr int kD4 = HD / 4;
+    // ranks polled together (bounds the registers; the FP32 kernels have fewer)
+    constexpr int kRG = Consumer::kElemBytes == 2 ? 4 : 2;
+    for (int it = tid; it < G * kD4; it += kNCT) {
+      const int hq = g * G + it / kD4, d = (it % kD4) * 4;
+      float M = -INFINITY, L = 0.f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int r0 = 0; r0 < W; r0 += kRG) {
+        uint64_t wv[kRG][6];  // per rank: o[d..d+3], m, l
+        unsigned long long t0 = 0;
+        for (;;) {
+          bool all = true;
+#pragma unroll
+          for (int u = 0; u < kRG; ++u) {
+            if (r0 + u < W) {
+              const uint64_t* rec =
+                  reinterpret_cast<const uint64_t*>(a.xch_local + xch_rec_offset(par, r0 + u)) +
+                  (int64_t)hq * kXR;
+              ld_relaxed_sys_u64x2(rec + d, wv[u][0], wv[u][1]);
+              ld_relaxed_sys_u64x2(rec + d + 2, wv[u][2], wv[u][3]);
+              ld_relaxed_sys_u64x2(rec + HD, wv[u][4], wv[u][5]);
+#pragma unroll
+              for (int e = 0; e < 6; ++e) all = all && (uint32_t)(wv[u][e] >> 32) == ep;
+            }
+          }
+          if (all || flags[0]) break;
+          if (t0 == 0) {
+            t0 = global_timer_ns();
+          } else if (global_timer_ns() - t0 > kWaitTimeoutNs) {
             flags[0] = 1;
             atomicCAS(a.status, 0, GLA_ERR_TIMEOUT);
             break;
           }
         }
-      }
-    }
-    consumer_sync(kNCT);
-    // one thread per (head, 4 columns); all of its loads in flight at once
-    constexpr int kXR = xch_row_floats<HD>();
-    constexpr int kD4 = HD / 4;
-    for (int it = tid; it < G * kD4; it += kNCT) {
-      const int hq = g * G + it / kD4, d = (it % kD4) * 4;
-      float2 ml[kXchMaxWorld];
-      float4 o[kXchMaxWorld];
+        // fold the group in with a running log-sum-exp
 #pragma unroll
-      for (int r = 0; r < kXchMaxWorld; ++r) {
-        if (r < W) {
-          const float* rec = reinterpret_cast<const float*>(a.xch_local + xch_rec_offset(par, r)) +
-                             (int64_t)hq * kXR;
-          ml[r] = __ldcg(reinterpret_cast<const float2*>(rec + HD));
-          o[r] = __ldcg(reinterpret_cast<const float4*>(rec + d));
-        } else {
-          ml[r] = make_float2(-INFINITY, 0.f);
-          o[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      }
-      float M = -INFINITY;
-#pragma unroll
-      for (int r = 0; r < kXchMaxWorld; ++r)
-        if (ml[r].y > 0.f) M = fmaxf(M, ml[r].x);
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      float L = 0.f;
-      if (M != -INFINITY) {
-#pragma unroll
-        for (int r = 0; r < kXchMaxWorld; ++r) {
-          if (ml[r].y > 0.f) {
-            const float w = ml[r].y * __expf(ml[r].x - M);
-            acc.x += w * o[r].x; acc.y += w * o[r].y; acc.z += w * o[r].z; acc.w += w * o[r].w;
-            L += w;
+        for (int u = 0; u < kRG; ++u) {
+          const float l = r0 + u < W ? __uint_as_float((uint32_t)wv[u][5]) : 0.f;
+          if (l > 0.f) {
+            const float m = __uint_as_float((uint32_t)wv[u][4]);
+            const float Mn = fmaxf(M, m);
+            const float sc = M == -INFINITY ? 0.f : __expf(M - Mn);
+            const float w = l * __expf(m - Mn);
+            acc.x = acc.x * sc + w * __uint_as_float((uint32_t)wv[u][0]);
+            acc.y = acc.y * sc + w * __uint_as_float((uint32_t)wv[u][1]);
+            acc.z = acc.z * sc + w * __uint_as_float((uint32_t)wv[u][2]);
+            acc.w = acc.w * sc + w * __uint_as_float((uint32_t)wv[u][3]);
+            L = L * sc + w;
+            M = Mn;
           }
         }
       }
@@ -891,8 +898,8 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
       epoch_read(g);
       consumer_sync(kNCT);
       for (int idx = tid; idx < G * HD; idx += kNCT)
-        write_final<HD>(a, b, g * G + idx / HD, idx % HD, 0.f, 0.f, 0.f, flags[2] & 1);
-      if (a.record_mode == 2) publish_merge(g);
+        write_final<HD, XCH>(a, b, g * G + idx / HD, idx % HD, 0.f, 0.f, 0.f, (uint32_t)flags[2]);
+      if constexpr (XCH) publish_merge(g);
     }
   }
   if (my_count == 0) return;
@@ -975,7 +982,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
         L = L * sa + Lo * sb;
         M = Mn;
       }
-      if (active && j == 0) write_final4<HD>(a, b, g * G + h, d, O, M, L, flags[2] & 1);
+      if (active && j == 0) write_final4<HD, XCH>(a, b, g * G + h, d, O, M, L, (uint32_t)flags[2]);
     }
   };
 
@@ -1009,7 +1016,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
         }
       }
       if (npieces == 1) {
-        write_final4<HD>(a, b, g * G + h, d, O, M, L, flags[2] & 1);
+        write_final4<HD, XCH>(a, b, g * G + h, d, O, M, L, (uint32_t)flags[2]);
       } else {
         float* slot = a.ws_part + ((int64_t)(blockIdx.x + s) * G + h) * kSH;
         *reinterpret_cast<float4*>(slot + d) = O;
@@ -1031,7 +1038,9 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
       }
     }
     consumer_sync(kNCT);
-    if (a.record_mode == 2 && merged_here) publish_merge(g);
+    if constexpr (XCH) {
+      if (merged_here) publish_merge(g);
+    }
   };
 
   // Piece by piece, tile by tile: the inner loop carries only the ring
