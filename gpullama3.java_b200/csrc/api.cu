@@ -115,6 +115,7 @@ int check_decode_shape(gla_ctx* ctx, int32_t n_heads, int32_t n_kv_heads, int32_
 }
 
 int run_decode(gla_ctx* ctx, gla::DecodeRequest& req) {
+  req.early_kv = ctx->opt_early_kv;  // every context entry point honours the option
   std::string err;
   gla::DecodePlan plan;
   int rc = gla::plan_decode(req, ctx->dev, &plan, &err);
@@ -156,7 +157,6 @@ int decode_single(gla_ctx* ctx, int dtype, const float* q, const void* k, const 
   req.scale = scale;
   req.out = out;
   req.record_mode = record_mode;
-  req.early_kv = ctx->opt_early_kv;
   return run_decode(ctx, req);
 }
 
@@ -292,7 +292,6 @@ int sharded(gla_ctx* ctx, int dtype, const float* q, const void* k, const void* 
     req.scale = scale;
     req.out = ctx->records;
     req.record_mode = 2;
-    req.early_kv = ctx->opt_early_kv;
     req.xch_bases = ctx->xch.bases();
     req.xch_local = ctx->xch.local();
     req.xch_out = xb;

@@ -27,6 +27,11 @@ __global__ void rope_append_f32_kernel(float* __restrict__ q, float* __restrict_
                                        int32_t n_kv_heads, int32_t head_dim,
                                        const int32_t* __restrict__ position_holder, double theta,
                                        int32_t style) {
+  // programmatic dependent launch: start behind the preceding kernel, touch
+  // memory only once it has finished, and let the following decode start
+  // (its early reads never cover the row or the q written here)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int pos = position_holder[0];
   const int half = head_dim / 2;
   const int64_t kv_dim = (int64_t)n_kv_heads * head_dim;
@@ -63,10 +68,19 @@ int launch_rope_append_f32(float* q, float* k, const float* v, float* key_cache,
                            int32_t rope_style, cudaStream_t stream, std::string* err) {
   const int n_pairs = n_heads * (head_dim / 2);
   const int threads = 128;
-  rope_append_f32_kernel<<<(n_pairs + threads - 1) / threads, threads, 0, stream>>>(
-      q, k, v, key_cache, value_cache, n_heads, n_kv_heads, head_dim, position_holder,
-      (double)theta, rope_style);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((n_pairs + threads - 1) / threads);
+  cfg.blockDim = dim3(threads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, rope_append_f32_kernel, q, k, v, key_cache,
+                                     value_cache, n_heads, n_kv_heads, head_dim, position_holder,
+                                     (double)theta, rope_style);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     *err = std::string("rope launch failed: ") + cudaGetErrorString(e);
     return GLA_ERR_CUDA;

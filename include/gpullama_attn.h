@@ -98,6 +98,9 @@ int32_t gla_num_sms(const gla_ctx* ctx);
  * issued just before them on the stream has finished - only if that kernel
  * releases its dependents early (griddepcontrol.launch_dependents); the
  * decode kernels of this library do, and never write caches or positions.
+ * (gla_rope_append_f32 also releases its dependents early; it writes q and
+ * only the cache row at the position holder, which a following decode over
+ * n_pos = position + 1 rows never reads early.)
  * What may be read early:
  *   1 - calls that take n_pos from the host (gla_decode_*,
  *       gla_decode_partial_*, gla_decode_sharded_*): K/V rows
