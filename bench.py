@@ -691,8 +691,9 @@ def run_e2e(args, ctx, wl, inp, torch, device, stream, dist):
             q = dev_in[l, : nh * hd]
             k = dev_in[l, nh * hd: nh * hd + kvd]
             v = dev_in[l, nh * hd + kvd:]
-            ctx.rope_append(q, k, v, K[l], V[l], nh, nkv, hd, pos, theta)
-            ctx.process_heads_flash_attention(q, K, V, xb[l], nh, hd, kvd, nh // nkv, pos, l, T)
+            # RoPE on q and the new key, KV append and attention: one launch
+            ctx.rope_append_attention(q, k, v, K, V, xb[l], nh, hd, kvd, nh // nkv, pos, l, T,
+                                      theta)
 
     # The per-token layer loop as a host plan replays it: captured once into a
     # CUDA graph (the position is read on the device, so the same graph serves
@@ -757,12 +758,12 @@ def run_e2e(args, ctx, wl, inp, torch, device, stream, dist):
             "h2d_bytes_per_step": int(host_in.numel() * 4),
             "d2h_bytes_per_step": int(host_out.numel() * 4),
             "path": "per step: pinned H2D of q/k/v rows, one CUDA-graph replay of "
-                    "gla_rope_append_f32 + gla_process_heads_flash_attention for every "
+                    "gla_rope_append_attention_f32 (RoPE + KV append + attention) for every "
                     "layer (captured once), pinned D2H of every xb",
             "eager": {"value": round(bytes_step / (ms_eager * 1e-3) / 1e9, 2),
                       "ms_per_step": round(ms_eager, 5),
                       "path": "the same calls issued eagerly from Python every step"},
-            "gpu_launches_per_step": 2 * L}
+            "gpu_launches_per_step": L}
 
 
 # ---------------------------------------------------------------------------

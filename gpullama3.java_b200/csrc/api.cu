@@ -197,10 +197,17 @@ int decode_batched(gla_ctx* ctx, int dtype, const float* q, const void* const* k
   return run_decode(ctx, req);
 }
 
+struct RopeAppend {
+  const float* k = nullptr;  // new key row [kvDim], unrotated
+  const float* v = nullptr;  // new value row [kvDim]
+  float theta = 0.f;
+  int32_t style = 0;
+};
+
 int process_heads(gla_ctx* ctx, int dtype, const float* q, const void* key_cache,
                   const void* value_cache, float* xb, int32_t n_heads, int32_t head_size,
                   int32_t kv_dim, int32_t kv_mul, const int32_t* position_holder, int32_t layer,
-                  int32_t context_length) {
+                  int32_t context_length, const RopeAppend* rope = nullptr) {
   if (!ctx) return GLA_ERR_INVALID_ARG;
   if (!q || !key_cache || !value_cache || !xb || !position_holder)
     return fail(ctx, GLA_ERR_INVALID_ARG, "null pointer");
@@ -236,6 +243,18 @@ int process_heads(gla_ctx* ctx, int dtype, const float* q, const void* key_cache
   req.scale = (float)(1.0 / std::sqrt((double)head_size));
   req.out = xb;
   req.record_mode = 0;
+  if (rope) {
+    if (!rope->k || !rope->v) return fail(ctx, GLA_ERR_INVALID_ARG, "null new key/value row");
+    if (rope->style != GLA_ROPE_INTERLEAVED && rope->style != GLA_ROPE_NEOX)
+      return fail(ctx, GLA_ERR_INVALID_ARG, "unknown rope_style");
+    if (!(rope->theta > 0.f) || !std::isfinite(rope->theta))
+      return fail(ctx, GLA_ERR_INVALID_ARG, "theta must be positive");
+    req.rope = 1;
+    req.rope_k = rope->k;
+    req.rope_v = rope->v;
+    req.rope_theta = (double)rope->theta;
+    req.rope_style = rope->style;
+  }
   return run_decode(ctx, req);
 }
 
@@ -485,6 +504,21 @@ int32_t gla_process_heads_flash_attention(gla_ctx* ctx, const float* q, const fl
                                           int32_t context_length) {
   return process_heads(ctx, GLA_DTYPE_F32, q, key_cache, value_cache, xb, n_heads, head_size,
                        kv_dim, kv_mul, position_holder, layer, context_length);
+}
+
+int32_t gla_rope_append_attention_f32(gla_ctx* ctx, const float* q, const float* k,
+                                      const float* v, float* key_cache, float* value_cache,
+                                      float* xb, int32_t n_heads, int32_t head_size,
+                                      int32_t kv_dim, int32_t kv_mul,
+                                      const int32_t* position_holder, int32_t layer,
+                                      int32_t context_length, float theta, int32_t rope_style) {
+  RopeAppend ra;
+  ra.k = k;
+  ra.v = v;
+  ra.theta = theta;
+  ra.style = rope_style;
+  return process_heads(ctx, GLA_DTYPE_F32, q, key_cache, value_cache, xb, n_heads, head_size,
+                       kv_dim, kv_mul, position_holder, layer, context_length, &ra);
 }
 
 int32_t gla_process_heads_flash_attention_f16kv(gla_ctx* ctx, const float* q,

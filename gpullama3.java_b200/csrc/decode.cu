@@ -38,7 +38,7 @@ int group_cap_for(int dtype, int group) {
 
 // Shared memory layout for a given tile/stage count.
 struct Layout {
-  int32_t off_bars, off_seq, off_q, off_pbuf, off_merge, off_flags;
+  int32_t off_bars, off_seq, off_q, off_pbuf, off_merge, off_flags, off_rope;
   size_t total;
 };
 
@@ -58,8 +58,9 @@ Layout layout_for(int dtype, int hd, int group, int tile, int stages, int batch,
   L.off_merge = (int32_t)align16(off);
   off = L.off_merge + (size_t)nw * group_cap_for(dtype, group) * (hd + 4) * sizeof(float);
   L.off_flags = (int32_t)align16(off);
+  L.off_rope = (int32_t)align16(L.off_flags + 16);
   (void)grid;
-  L.total = L.off_flags + 16 + 1024;  // + slack to 1024-align the stage ring
+  L.total = L.off_rope + (size_t)(hd / 2) * 8 + 1024;  // + slack to 1024-align the stage ring
   return L;
 }
 
@@ -275,6 +276,12 @@ int launch_decode(const DecodeRequest& r, const DecodePlan& p, float* ws_part, i
   a.off_q = L.off_q;
   a.off_merge = L.off_merge;
   a.off_flags = L.off_flags;
+  a.off_rope = L.off_rope;
+  a.rope = r.rope;
+  a.rope_style = r.rope_style;
+  a.rope_theta = r.rope_theta;
+  a.rope_k = r.rope_k;
+  a.rope_v = r.rope_v;
   // the peer exchange (record mode 2: one sequence, tensor-map loader) is a
   // separate instantiation, so the other kernels carry none of its registers
   cudaError_t rc = r.record_mode == 2 && loader == 0 ? launch_any<0, true>(r.dtype, hd, a, p, stream)

@@ -42,6 +42,7 @@
 #pragma once
 
 #include "gla_common.cuh"
+#include "gla_rope.cuh"
 #include "gla_xch.h"
 
 namespace gla {
@@ -78,6 +79,15 @@ struct DecodeArgs {
   float* xch_out;              // mode 2: merged xb [n_heads][HD]
   int32_t xch_world;
   int32_t xch_rank;
+  // fused RoPE + append (rope != 0: one sequence, FP32 cache, tensor-map
+  // loader): the new token's key row is rotated and written, with its value
+  // row, at row n_pos - 1 of the caches before that row's tile is loaded; q
+  // is rotated on its way into shared memory
+  const float* rope_k;         // [n_kv * HD] new key, unrotated
+  const float* rope_v;         // [n_kv * HD] new value
+  double rope_theta;
+  int32_t rope;
+  int32_t rope_style;
   float* ws_part;              // workspace slots [P + B*n_kv][G][HD+4] (o, m, l, pad)
   int32_t* ws_counter;         // [B*n_kv], zero between calls
   int32_t* status;             // device status word
@@ -89,6 +99,7 @@ struct DecodeArgs {
   int32_t off_q;               // the group's q vectors [kMaxGroup][HD]
   int32_t off_merge;
   int32_t off_flags;
+  int32_t off_rope;            // float2 [HD/2]: (cos, sin) of the new position
 };
 
 // Floats per head in a workspace piece slot: o[HD], m, l, 2 pad (16-byte rows).
@@ -643,6 +654,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   float* pbuf = reinterpret_cast<float*>(smem + a.off_pbuf);           // [NW][kPbufFloats]
   float* merge = reinterpret_cast<float*>(smem + a.off_merge);         // [NW][kMG][HD+4]
   volatile int* flags = reinterpret_cast<volatile int*>(smem + a.off_flags);  // [0]=abort [1]=last
+  float2* rope_cs = reinterpret_cast<float2*>(smem + a.off_rope);      // [HD/2] (fused RoPE)
 
   if (tid == 0) {
     for (int s = 0; s < a.stages; ++s) {
@@ -688,6 +700,43 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
       if (lane == 0) seq_start[B] = carry * n_kv;
     }
   };
+  // Fused RoPE: (cos, sin) of every pair at the new position (row n_pos - 1
+  // of the one sequence), computed once per CTA.
+  auto rope_table = [&]() {
+    if (!a.rope) return;
+    const int pos = npos[0] - 1;
+    for (int i = tid; i < HD / 2; i += blockDim.x) {
+      float c, sn;
+      rope_cos_sin(pos, i, HD, a.rope_theta, &c, &sn);
+      rope_cs[i] = make_float2(c, sn);
+    }
+  };
+  // Fused RoPE + append, producer warp: kv head g's new key row (rotated)
+  // and value row are written at row n_pos - 1 of the caches, then a proxy
+  // fence orders those generic stores before the tensor copy that reads the
+  // row back (only the CTA holding that row's tile does this).
+  auto append_row = [&](int g) {
+    const int pos = npos[0] - 1;
+    float* kc = const_cast<float*>(static_cast<const float*>(a.k)) + (int64_t)pos * a.kv_stride +
+                (int64_t)g * HD;
+    float* vc = const_cast<float*>(static_cast<const float*>(a.v)) + (int64_t)pos * a.kv_stride +
+                (int64_t)g * HD;
+    const float* kn = a.rope_k + (int64_t)g * HD;
+    const float* vn = a.rope_v + (int64_t)g * HD;
+    for (int ic = lane; ic < HD / 2; ic += 32) {
+      int i0, i1;
+      rope_pair(a.rope_style, ic, HD, &i0, &i1);
+      const float2 cs = rope_cs[ic];
+      float o0, o1;
+      rope_rotate(kn[i0], kn[i1], cs.x, cs.y, &o0, &o1);
+      kc[i0] = o0;
+      kc[i1] = o1;
+      vc[i0] = vn[i0];
+      vc[i1] = vn[i1];
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __syncwarp();
+  };
   // TMA loads of one tile (LOADER 0): whole boxes of `tile` rows; rows past
   // the tensor map's extent are zero-filled, so the byte count is the boxes'
   // size.  Rows past n_pos inside the extent are loaded and masked later.
@@ -723,6 +772,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   if (early) {
     scan_sequences();
     __syncthreads();
+    rope_table();  // the position is known: overlap the double-precision work too
     if (warp == NW && lane == 0) {
       const Deal d0 = make_deal(seq_start[B], (int32_t)gridDim.x, B, n_kv, nunits[0]);
       int32_t lo, cnt;
@@ -744,6 +794,10 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   pdl_launch_dependents();
   if (!early) scan_sequences();
   __syncthreads();
+  if (!early && a.rope) {
+    rope_table();
+    __syncthreads();
+  }
 
   const int32_t W = seq_start[B];
   const Deal deal = make_deal(W, (int32_t)gridDim.x, B, n_kv, nunits[0]);
@@ -761,7 +815,10 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
       Tile t;
       for (int32_t k = 0; k < first; ++k) {  // first ring pass: no empty-barrier waits
         wk.next(nunits, B, n_kv, tile_units, unit_rows, t);
-        if (lane == 0 && ((late_mask >> k) & 1u)) tma_tile(k, t, pol);
+        if ((late_mask >> k) & 1u) {
+          if (a.rope) append_row(t.g);
+          if (lane == 0) tma_tile(k, t, pol);
+        }
       }
       __syncwarp();
       int cur_b = -1;
@@ -772,6 +829,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
       for (; wk.next(nunits, B, n_kv, tile_units, unit_rows, t);) {
         if (!mbar_wait(&empty[st], phase, flags, a.status)) break;
         if constexpr (LOADER == 0) {
+          if (a.rope && t.row0 + t.units * unit_rows >= npos[t.b]) append_row(t.g);
           if (lane == 0) tma_tile(st, t, pol);
           __syncwarp();
         } else {
@@ -913,7 +971,22 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   // The group's q vectors, pre-scaled by scale*log2(e), rows >= G zeroed.
   auto load_q = [&](int b, int g) {
     const float* qb = a.q + ((int64_t)b * a.n_heads + (int64_t)g * G) * HD;
-    for (int i = tid; i < kMaxGroup * HD; i += kNCT) qs[i] = i < G * HD ? qb[i] * a.q_scale : 0.f;
+    if (a.rope) {  // fused RoPE: rotate on the way in (the caller's q stays as it was)
+      for (int p = tid; p < kMaxGroup * (HD / 2); p += kNCT) {
+        const int h = p / (HD / 2), ic = p - h * (HD / 2);
+        int i0, i1;
+        rope_pair(a.rope_style, ic, HD, &i0, &i1);
+        float o0 = 0.f, o1 = 0.f;
+        if (h < G) {
+          const float2 cs = rope_cs[ic];
+          rope_rotate(qb[h * HD + i0], qb[h * HD + i1], cs.x, cs.y, &o0, &o1);
+        }
+        qs[h * HD + i0] = o0 * a.q_scale;
+        qs[h * HD + i1] = o1 * a.q_scale;
+      }
+    } else {
+      for (int i = tid; i < kMaxGroup * HD; i += kNCT) qs[i] = i < G * HD ? qb[i] * a.q_scale : 0.f;
+    }
     consumer_sync(kNCT);
   };
 

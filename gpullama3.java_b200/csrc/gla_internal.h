@@ -37,6 +37,12 @@ struct DecodeRequest {
   float* xch_out = nullptr;
   int32_t xch_world = 0;
   int32_t xch_rank = 0;
+  // fused RoPE + append (FP32 cache, one sequence, device position)
+  int32_t rope = 0;
+  int32_t rope_style = 0;
+  double rope_theta = 0.0;
+  const float* rope_k = nullptr;
+  const float* rope_v = nullptr;
 };
 
 // Launch geometry chosen for a request.

@@ -12,13 +12,12 @@
 // and sums so no FMA changes the result.
 #include "gla_common.cuh"
 #include "gla_internal.h"
+#include "gla_rope.cuh"
 
 namespace gla {
 
 __device__ __forceinline__ void rotate_pair(float* x, int i0, int i1, float fcr, float fci) {
-  const float v0 = x[i0], v1 = x[i1];
-  x[i0] = __fsub_rn(__fmul_rn(v0, fcr), __fmul_rn(v1, fci));
-  x[i1] = __fadd_rn(__fmul_rn(v0, fci), __fmul_rn(v1, fcr));
+  rope_rotate(x[i0], x[i1], fcr, fci, &x[i0], &x[i1]);
 }
 
 __global__ void rope_append_f32_kernel(float* __restrict__ q, float* __restrict__ k,
@@ -39,18 +38,12 @@ __global__ void rope_append_f32_kernel(float* __restrict__ q, float* __restrict_
   const int n_pairs = n_heads * half;
   if (idx < n_pairs) {
     const int h = idx / half, ic = idx - h * half;
-    const float freq = (float)(1.0 / pow(theta, (double)(2 * ic) / (double)head_dim));
-    const float ang = __fmul_rn((float)pos, freq);
-    const float fcr = (float)cos((double)ang);
-    const float fci = (float)sin((double)ang);
+    float fcr, fci;
+    rope_cos_sin(pos, ic, head_dim, theta, &fcr, &fci);
     int i0, i1;
-    if (style == GLA_ROPE_INTERLEAVED) {
-      i0 = h * head_dim + 2 * ic;
-      i1 = i0 + 1;
-    } else {
-      i0 = h * head_dim + ic;
-      i1 = i0 + half;
-    }
+    rope_pair(style, ic, head_dim, &i0, &i1);
+    i0 += h * head_dim;
+    i1 += h * head_dim;
     rotate_pair(q, i0, i1, fcr, fci);
     if (h < n_kv_heads) {
       rotate_pair(k, i0, i1, fcr, fci);

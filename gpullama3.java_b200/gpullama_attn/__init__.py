@@ -76,6 +76,8 @@ _SIGS = {
     "gla_debug_partition": (_I64, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P,
                                    _P, _P, _I64]),
     "gla_comm_peer_exchange": (_I32, [_P]),
+    "gla_rope_append_attention_f32": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32,
+                                             _P, _I32, _I32, _F, _I32]),
     "gla_decode_f32kv_noalloc": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F, _P]),
 }
 
@@ -293,6 +295,15 @@ class Context:
         self._check(self._L.gla_prefill_causal_f16(self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(out),
                                                    L, n_heads, n_kv_heads, head_dim, scale),
                     "gla_prefill_causal_f16")
+
+    def rope_append_attention(self, q, k, v, key_cache, value_cache, xb, n_heads, head_size,
+                              kv_dim, kv_mul, position_holder, layer, context_length, theta,
+                              style=ROPE_INTERLEAVED):
+        """gla_rope_append_attention_f32: RoPE + KV append + attention, one launch."""
+        self._check(self._L.gla_rope_append_attention_f32(
+            self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(key_cache), _ptr(value_cache), _ptr(xb),
+            n_heads, head_size, kv_dim, kv_mul, _ptr(position_holder), layer, context_length,
+            theta, style), "gla_rope_append_attention_f32")
 
     def rope_append(self, q, k, v, key_cache, value_cache, n_heads, n_kv_heads, head_dim,
                     position_holder, theta, style=ROPE_INTERLEAVED):

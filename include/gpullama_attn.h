@@ -159,6 +159,21 @@ int32_t gla_process_heads_flash_attention(gla_ctx* ctx, const float* q, const fl
                                           const int32_t* position_holder, int32_t layer,
                                           int32_t context_length);
 
+/* One layer's attention step of a token in one launch: RoPE on q and on
+ * the new key (as gla_rope_append_f32), the new key and value rows written
+ * at row `position` of this layer's caches, then the attention of
+ * gla_process_heads_flash_attention over rows 0..position -- the same bits
+ * as those two calls in a row.  q and k are read, not rotated in place.
+ * Replaces the rope, copyToCache and parallel-attention tasks of one layer
+ * (TransformerComputeKernelsLayered.java:129-139, :179-205, :336-458); no
+ * single reference counterpart.  k, v: [kvDim] rows of the new token. */
+int32_t gla_rope_append_attention_f32(gla_ctx* ctx, const float* q, const float* k,
+                                      const float* v, float* key_cache, float* value_cache,
+                                      float* xb, int32_t n_heads, int32_t head_size,
+                                      int32_t kv_dim, int32_t kv_mul,
+                                      const int32_t* position_holder, int32_t layer,
+                                      int32_t context_length, float theta, int32_t rope_style);
+
 /* Same task over an FP16 cache (new capability; the reference KV is FP32). */
 int32_t gla_process_heads_flash_attention_f16kv(gla_ctx* ctx, const float* q,
                                                 const uint16_t* key_cache,

@@ -335,3 +335,46 @@ def test_early_prefetch_sees_the_row_appended_just_before(gla_ctx, oracle):
     np.testing.assert_array_equal(outs[0], outs[1])
     np.testing.assert_array_equal(outs[0], outs[2])
     np.testing.assert_array_equal(outs_dev[0], outs_dev[2])
+
+
+@pytest.mark.parametrize("style,hd,nh,nkv", [(0, 128, 24, 8), (1, 96, 32, 32), (0, 64, 32, 8),
+                                             (1, 128, 28, 4)])
+def test_fused_rope_append_attention_equals_separate_calls(gla_ctx, style, hd, nh, nkv):
+    """gla_rope_append_attention_f32 = gla_rope_append_f32 followed by
+    gla_process_heads_flash_attention, bit for bit: the output, the written
+    cache row (and nothing else), and the caller's q left unrotated.  Run
+    behind back-to-back decodes so its early history reads overlap them."""
+    import gpullama_attn as gla
+
+    torch = _torch()
+    n_layers, ctxlen, pos, layer, theta = 2, 700, 515, 1, 500000.0
+    kvd = nkv * hd
+    rng = np.random.Generator(np.random.PCG64(77 + hd + style))
+    kc0 = rng.standard_normal((n_layers, ctxlen, kvd), dtype=np.float32)
+    vc0 = rng.standard_normal((n_layers, ctxlen, kvd), dtype=np.float32)
+    q0 = rng.standard_normal(nh * hd, dtype=np.float32)
+    k0 = rng.standard_normal(kvd, dtype=np.float32)
+    v0 = rng.standard_normal(kvd, dtype=np.float32)
+    ph = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    kc1, vc1, q1, k1, v1 = dev(kc0), dev(vc0), dev(q0), dev(k0), dev(v0)
+    xb1 = torch.empty(nh * hd, device="cuda")
+    gla_ctx.rope_append(q1, k1, v1, kc1[layer], vc1[layer], nh, nkv, hd, ph, theta, style)
+    gla_ctx.process_heads_flash_attention(q1, kc1, vc1, xb1, nh, hd, kvd, nh // nkv, ph, layer,
+                                          ctxlen)
+    kc2, vc2, q2, k2, v2 = dev(kc0), dev(vc0), dev(q0), dev(k0), dev(v0)
+    xb2 = torch.empty(nh * hd, device="cuda")
+    scratch = torch.empty(nh * hd, device="cuda")
+    for _ in range(3):  # decodes that release their dependents early
+        gla_ctx.decode(q2, kc2[0], vc2[0], scratch, nh, nkv, hd, ctxlen)
+    gla_ctx.rope_append_attention(q2, k2, v2, kc2, vc2, xb2, nh, hd, kvd, nh // nkv, ph, layer,
+                                  ctxlen, theta, style)
+    assert gla_ctx.device_status() == 0
+    np.testing.assert_array_equal(xb2.cpu().numpy(), xb1.cpu().numpy())
+    np.testing.assert_array_equal(kc2.cpu().numpy(), kc1.cpu().numpy())
+    np.testing.assert_array_equal(vc2.cpu().numpy(), vc1.cpu().numpy())
+    np.testing.assert_array_equal(q2.cpu().numpy(), q0)
+    changed = np.argwhere(np.any(kc2.cpu().numpy() != kc0, axis=-1))
+    assert changed.tolist() == [[layer, pos]]
+    with pytest.raises(gla.GlaError):
+        gla_ctx.rope_append_attention(q2, k2, v2, kc2, vc2, xb2, nh, hd, kvd, nh // nkv, ph,
+                                      layer, ctxlen, theta, 7)
