@@ -985,7 +985,20 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
         qs[h * HD + i1] = o1 * a.q_scale;
       }
     } else {
-      for (int i = tid; i < kMaxGroup * HD; i += kNCT) qs[i] = i < G * HD ? qb[i] * a.q_scale : 0.f;
+      // all of a thread's loads first: one memory round trip on the critical
+      // path of every piece, not one per element
+      constexpr int kPer = (kMaxGroup * HD + kNCT - 1) / kNCT;
+      float v[kPer];
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        const int i = tid + u * kNCT;
+        v[u] = i < G * HD ? __ldg(qb + i) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        const int i = tid + u * kNCT;
+        if (i < kMaxGroup * HD) qs[i] = v[u] * a.q_scale;
+      }
     }
     consumer_sync(kNCT);
   };
