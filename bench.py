@@ -607,39 +607,65 @@ def run_prefill(args, rank, world, local_rank, dist):
         ms = float(t.item())
     if ctx.device_status() != 0:
         raise RuntimeError("device status after the timed region")
-    flops = 4.0 * nh * hd * L * (L + 1) / 2
-    tflops = flops / (ms * 1e-3) / 1e12 * world
+    tflops = 4.0 * nh * hd * L * (L + 1) / 2 / (ms * 1e-3) / 1e12 * world
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
             pk = json.load(f)
         peak, peak_kind = float(pk["bf16_tflops"]), "measured cuBLAS bf16 burst (MEASURED_PEAKS.json)"
     except Exception:
         peak, peak_kind = 1590.0, "fallback 1.59 PFLOP/s"
-    # e2e: pinned host Q/K/V in, output back, through the C ABI
-    hq = q.cpu().pin_memory()
-    hk = k.cpu().pin_memory()
-    hv = v.cpu().pin_memory()
+    flops = 4.0 * nh * hd * L * (L + 1) / 2
+
+    def timed(fn):
+        """Warm-up, then device time per call (ms), bounded below by wall time."""
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                fn()
+            torch.cuda.synchronize(device)
+            w0 = time.perf_counter()
+            e0.record(stream)
+            for _ in range(args.steps):
+                fn()
+            e1.record(stream)
+        torch.cuda.synchronize(device)
+        return max(e0.elapsed_time(e1), (time.perf_counter() - w0) * 1e3) / args.steps
+
+    # e2e through the reference-facing call: the prompt's FP32 q/k/v rows (a
+    # batched QKV projection's output, before RoPE) from pinned host memory,
+    # gla_ingest_prompt_f32 (RoPE, append to an FP32 [ctx][kv_dim] layer cache,
+    # causal attention), xb back to pinned host memory
+    g32 = torch.Generator(device="cpu").manual_seed(2000 + rank)
+    hq = torch.randn(L, nh * hd, generator=g32).pin_memory()
+    hk = torch.randn(L, nkv * hd, generator=g32).pin_memory()
+    hv = torch.randn(L, nkv * hd, generator=g32).pin_memory()
     hout = torch.empty(L, nh * hd).pin_memory()
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    with torch.cuda.stream(stream):
+        dq, dk, dv = (torch.empty(x.shape, device=device) for x in (hq, hk, hv))
+        kc32 = torch.zeros(L, nkv * hd, device=device)
+        vc32 = torch.zeros_like(kc32)
+        kc16 = torch.zeros(L, nkv * hd, device=device, dtype=torch.float16)
+        vc16 = torch.zeros_like(kc16)
+    theta = 10000.0
 
     def e2e_step():
         dq.copy_(hq, non_blocking=True)
         dk.copy_(hk, non_blocking=True)
         dv.copy_(hv, non_blocking=True)
-        ctx.prefill_causal(dq, dk, dv, out, L, nh, nkv, hd)
+        ctx.ingest_prompt(dq, dk, dv, kc32, vc32, out, 0, L, nh, nkv, hd, L, theta,
+                          gla.ROPE_NEOX)
         hout.copy_(out, non_blocking=True)
 
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            e2e_step()
-        torch.cuda.synchronize(device)
-        w0 = time.perf_counter()
-        e0.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
-        e1.record(stream)
-    torch.cuda.synchronize(device)
-    e2e_ms = max(e0.elapsed_time(e1), (time.perf_counter() - w0) * 1e3) / args.steps
+    e2e_ms = timed(e2e_step)
+
+    # the same prompt ingestion with device-resident inputs, both cache types
+    def ingest(kc, vc, f16):
+        return lambda: ctx.ingest_prompt(dq, dk, dv, kc, vc, out, 0, L, nh, nkv, hd, L, theta,
+                                         gla.ROPE_NEOX, f16_cache=f16)
+
+    ing32_ms = timed(ingest(kc32, vc32, False))
+    ing16_ms = timed(ingest(kc16, vc16, True))
+    if ctx.device_status() != 0:
+        raise RuntimeError("device status after the ingestion runs")
     res = {
         "metric": "prefill-attn TFLOP/s (causal)", "value": round(tflops, 2), "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -659,8 +685,14 @@ def run_prefill(args, rank, world, local_rank, dist):
         "clocks": dict(clocks, soak_s=round(soak_s, 2)) if clocks else None,
         "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12 * world, 2), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 4),
-                "h2d_bytes_per_step": int((q.numel() + k.numel() + v.numel()) * 2),
-                "d2h_bytes_per_step": int(out.numel() * 4)},
+                "call": "gla_ingest_prompt_f32 (RoPE + FP32 KV append + causal attention)",
+                "h2d_bytes_per_step": int((hq.numel() + hk.numel() + hv.numel()) * 4),
+                "d2h_bytes_per_step": int(hout.numel() * 4)},
+        "ingest": {"unit": "TFLOP/s", "note": "device-resident FP32 q/k/v, RoPE + append + "
+                   "attention of the whole prompt in one call",
+                   "f32_cache": round(flops / (ing32_ms * 1e-3) / 1e12, 2),
+                   "f16_cache": round(flops / (ing16_ms * 1e-3) / 1e12, 2),
+                   "f32_cache_ms": round(ing32_ms, 4), "f16_cache_ms": round(ing16_ms, 4)},
     }
     if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.quick):
         res["cpu_baseline"] = cpu_prefill_sample(wl)

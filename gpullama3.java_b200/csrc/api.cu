@@ -31,6 +31,8 @@ struct gla_ctx {
   float* records = nullptr;         // sharded decode: local records
   float* gathered = nullptr;        // sharded decode: all ranks' records
   size_t records_cap = 0;           // floats per rank
+  uint16_t* ingest_ws = nullptr;    // prompt ingestion: FP16 q (and K/V) copies
+  size_t ingest_cap = 0;            // halves
   gla::Comm comm;
   gla::PeerExchange xch;            // sharded decode: peer exchange buffers
   int32_t opt_early_kv = 2;         // GLA_OPT_EARLY_KV_PREFETCH
@@ -403,6 +405,7 @@ int32_t gla_destroy(gla_ctx* ctx) {
     cudaFree(ctx->parts);
     cudaFree(ctx->records);
     cudaFree(ctx->gathered);
+    cudaFree(ctx->ingest_ws);
   }
   delete ctx;
   return GLA_OK;
@@ -647,8 +650,9 @@ int32_t gla_prefill_causal_f16(gla_ctx* ctx, const uint16_t* q, const uint16_t* 
     return fail(ctx, GLA_ERR_ALIGNMENT, "prefill tensors must be 16-byte aligned");
   DeviceGuard dg(ctx->device);
   std::string err;
-  int rc = gla::launch_prefill_f16(q, k, v, out, L, n_heads, n_kv_heads, head_dim, scale,
-                                   ctx->status, ctx->dev, ctx->stream, &err);
+  int rc = gla::launch_prefill_f16(q, k, v, out, L, 0, (int64_t)n_kv_heads * head_dim, n_heads,
+                                   n_kv_heads, head_dim, scale, ctx->status, ctx->dev,
+                                   ctx->stream, &err);
   return rc == GLA_OK ? GLA_OK : fail(ctx, rc, err);
 }
 
@@ -670,6 +674,73 @@ int32_t gla_rope_append_f32(gla_ctx* ctx, float* q, float* k, const float* v, fl
                                        head_dim, position_holder, theta, rope_style, ctx->stream,
                                        &err);
   return rc == GLA_OK ? GLA_OK : fail(ctx, rc, err);
+}
+
+namespace {
+
+int ingest_prompt(gla_ctx* ctx, bool f16_cache, const float* q, const float* k, const float* v,
+                  void* key_cache, void* value_cache, float* xb, int32_t start_pos,
+                  int32_t n_rows, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                  int32_t context_length, float theta, int32_t rope_style) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  if (!q || !k || !v || !key_cache || !value_cache || !xb)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "null pointer");
+  if (n_rows < 1 || n_heads < 1 || n_kv_heads < 1 || n_heads % n_kv_heads != 0)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "bad ingestion shape");
+  if (head_dim != 64 && head_dim != 96 && head_dim != 128)
+    return fail(ctx, GLA_ERR_NOT_SUPPORTED, "prompt ingestion head_dim must be 64, 96 or 128");
+  if (start_pos < 0 || context_length < 1 || (int64_t)start_pos + n_rows > context_length)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "positions past context_length");
+  if (rope_style != GLA_ROPE_INTERLEAVED && rope_style != GLA_ROPE_NEOX)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "unknown rope_style");
+  if (!(theta > 0.f)) return fail(ctx, GLA_ERR_INVALID_ARG, "theta must be positive");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(key_cache) ||
+      !aligned16(value_cache))
+    return fail(ctx, GLA_ERR_ALIGNMENT, "q, k, v and the caches must be 16-byte aligned");
+  DeviceGuard dg(ctx->device);
+  const size_t need = gla::ingest_workspace_halves(f16_cache, start_pos, n_rows, n_heads,
+                                                   n_kv_heads, head_dim);
+  if (need > ctx->ingest_cap) {
+    if (stream_capturing(ctx->stream))
+      return fail(ctx, GLA_ERR_INVALID_ARG,
+                  "ingestion workspace must grow; run the largest call once before capture");
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamSynchronize");
+    cudaFree(ctx->ingest_ws);
+    ctx->ingest_ws = nullptr;
+    ctx->ingest_cap = 0;
+    e = cudaMalloc(&ctx->ingest_ws, need * sizeof(uint16_t));
+    if (e != cudaSuccess) {
+      ctx->ingest_ws = nullptr;
+      return cuda_fail(ctx, e, "cudaMalloc ingestion workspace");
+    }
+    ctx->ingest_cap = need;
+  }
+  std::string err;
+  int rc = gla::launch_ingest(f16_cache, q, k, v, key_cache, value_cache, xb, ctx->ingest_ws,
+                              start_pos, n_rows, n_heads, n_kv_heads, head_dim, theta,
+                              rope_style, ctx->status, ctx->dev, ctx->stream, &err);
+  return rc == GLA_OK ? GLA_OK : fail(ctx, rc, err);
+}
+
+}  // namespace
+
+int32_t gla_ingest_prompt_f32(gla_ctx* ctx, const float* q, const float* k, const float* v,
+                              float* key_cache, float* value_cache, float* xb, int32_t start_pos,
+                              int32_t n_rows, int32_t n_heads, int32_t n_kv_heads,
+                              int32_t head_dim, int32_t context_length, float theta,
+                              int32_t rope_style) {
+  return ingest_prompt(ctx, false, q, k, v, key_cache, value_cache, xb, start_pos, n_rows,
+                       n_heads, n_kv_heads, head_dim, context_length, theta, rope_style);
+}
+
+int32_t gla_ingest_prompt_f16kv(gla_ctx* ctx, const float* q, const float* k, const float* v,
+                                uint16_t* key_cache, uint16_t* value_cache, float* xb,
+                                int32_t start_pos, int32_t n_rows, int32_t n_heads,
+                                int32_t n_kv_heads, int32_t head_dim, int32_t context_length,
+                                float theta, int32_t rope_style) {
+  return ingest_prompt(ctx, true, q, k, v, key_cache, value_cache, xb, start_pos, n_rows,
+                       n_heads, n_kv_heads, head_dim, context_length, theta, rope_style);
 }
 
 int64_t gla_debug_partition(const int32_t* n_pos, int32_t n_seq, int32_t n_kv_heads, int32_t tile,

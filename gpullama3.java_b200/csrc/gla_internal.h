@@ -80,10 +80,22 @@ int launch_rope_append_f32(float* q, float* k, const float* v, float* key_cache,
                            int32_t head_dim, const int32_t* position_holder, float theta,
                            int32_t rope_style, cudaStream_t stream, std::string* err);
 
-// Causal prefill (tcgen05).
+// Causal prefill (tcgen05): L query rows at positions q_off..q_off+L-1 over
+// key/value rows 0..q_off+L-1 (row stride kv_stride halves).
 int launch_prefill_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v, float* out,
-                       int32_t L, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
-                       float scale, int32_t* status, const DeviceInfo& dev, cudaStream_t stream,
-                       std::string* err);
+                       int32_t L, int32_t q_off, int64_t kv_stride, int32_t n_heads,
+                       int32_t n_kv_heads, int32_t head_dim, float scale, int32_t* status,
+                       const DeviceInfo& dev, cudaStream_t stream, std::string* err);
+
+// Batched prompt ingestion of one layer (ingest.cu): RoPE, KV append and
+// causal attention of n_rows positions from start_pos.  ws holds
+// ingest_workspace_halves(...) halves, 16-byte aligned.
+size_t ingest_workspace_halves(bool f16_cache, int32_t start_pos, int32_t n_rows,
+                               int32_t n_heads, int32_t n_kv_heads, int32_t head_dim);
+int launch_ingest(bool f16_cache, const float* q, const float* k, const float* v, void* key_cache,
+                  void* value_cache, float* xb, uint16_t* ws, int32_t start_pos, int32_t n_rows,
+                  int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, float theta,
+                  int32_t rope_style, int32_t* status, const DeviceInfo& dev,
+                  cudaStream_t stream, std::string* err);
 
 }  // namespace gla

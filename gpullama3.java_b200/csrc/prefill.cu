@@ -50,11 +50,12 @@ constexpr float kRescaleLog2 = 8.0f;
 constexpr int kPolyPairs = 0;
 
 struct PrefillArgs {
-  CUtensorMap tq;  // [L][n_heads*hd]    box (32, 128), SWIZZLE_64B
-  CUtensorMap tk;  // [L][n_kv*hd]       box (32, 128)
+  CUtensorMap tq;  // [L][n_heads*hd]           box (32, 128), SWIZZLE_64B
+  CUtensorMap tk;  // [q_off+L][n_kv*hd], rows kv_stride apart; box (32, 128)
   CUtensorMap tv;
   float* out;      // [L][n_heads*hd] FP32
-  int32_t L;
+  int32_t L;       // query rows
+  int32_t q_off;   // position of query row 0: row i attends keys 0..q_off+i
   int32_t n_heads;
   int32_t kv_mul;
   int32_t n_qblocks;
@@ -264,7 +265,10 @@ __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
   const int qb = a.n_qblocks - 1 - (int)(blockIdx.x / a.n_heads);
   const int h = (int)(blockIdx.x % a.n_heads);
   const int g = h / a.kv_mul;
-  const int nb_last = (qb * NT + NT - 1) + 1;  // key blocks of the last tile
+  // key blocks of query tile qt: through the block holding the position of
+  // its last row below L (rows past L are computed but never stored)
+  auto tile_blocks = [&](int qt) { return (a.q_off + imin(qt * kBM + kBM, a.L) - 1) / kBN + 1; };
+  const int nb_last = tile_blocks(qb * NT + NT - 1);  // key blocks of the last tile
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kOffBar);
   uint64_t* q_full = bars;
@@ -387,7 +391,7 @@ __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
           ok = ok && mbar_wait(&k_full[(j + 1) % KS], (uint32_t)(((j + 1) / KS) & 1), abort_flag,
                                a.status);
         for (int t = 0; t < NT; ++t) {
-          const int nb_t = qb * NT + t + 1;
+          const int nb_t = tile_blocks(qb * NT + t);
           if (j >= nb_t) continue;
           // S_t(j+1) first: the tile's next softmax waits on it, while
           // P_t(j) V_j is needed only before P_t(j+1) is written
@@ -415,8 +419,9 @@ __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
     const int t = warp >> 2;                  // query tile of this warpgroup
     const int r = tid & 127;                  // row inside the tile (== TMEM lane)
     const int qt = qb * NT + t;               // global 128-row block of the tile
-    const int qi = qt * kBM + r;              // query position
-    const int nb = qt + 1;                    // causal key blocks of this tile
+    const int qi = qt * kBM + r;              // query row
+    const int qpos = a.q_off + qi;            // its position: keys 0..qpos
+    const int nb = tile_blocks(qt);           // causal key blocks of this tile
     const uint32_t lane_sel = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + 256 * t + lane_sel;
     const uint32_t tO = tS + 128;
@@ -429,8 +434,9 @@ __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
       mbar_wait(&s_full[t], (uint32_t)(j & 1), abort_flag, a.status);
       tc_fence_after();
       // pass 1: row max of the raw scores, two 64-column halves (4 chains);
-      // the causal mask only touches the diagonal block
-      const bool diag = (j == qt);
+      // the causal mask only touches blocks holding a key past the tile's
+      // first position (the diagonal block, two when q_off % 128 != 0)
+      const bool diag = j * kBN + kBN - 1 > a.q_off + qt * kBM;
       float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
@@ -439,7 +445,7 @@ __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
         if (diag) {
 #pragma unroll
           for (int c = 0; c < 64; ++c)
-            if (j * kBN + hh * 64 + c > qi) s[c] = -INFINITY;
+            if (j * kBN + hh * 64 + c > qpos) s[c] = -INFINITY;
         }
 #pragma unroll
         for (int c = 0; c < 64; c += 8) {
@@ -484,7 +490,7 @@ __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
         if (diag) {
 #pragma unroll
           for (int c = 0; c < 64; ++c)
-            if (j * kBN + hh * 64 + c > qi) s[c] = -INFINITY;
+            if (j * kBN + hh * 64 + c > qpos) s[c] = -INFINITY;
         }
 #pragma unroll
         for (int ch = 0; ch < 8; ++ch) {  // 16-byte chunks of 8 keys
@@ -562,14 +568,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn_prefill() {
 }
 
 bool encode_f16_rows(CUtensorMap* map, const void* base, int64_t width, int64_t rows,
-                     std::string* err) {
+                     int64_t stride, std::string* err) {
   auto fn = encode_fn_prefill();
   if (!fn) {
     *err = "cuTensorMapEncodeTiled unavailable";
     return false;
   }
   cuuint64_t dims[2] = {(cuuint64_t)width, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(width * 2)};
+  cuuint64_t strides[1] = {(cuuint64_t)(stride * 2)};
   cuuint32_t box[2] = {32, 128};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
@@ -602,9 +608,9 @@ int launch_hd(PrefillArgs a, cudaStream_t stream, std::string* err) {
 }  // namespace
 
 int launch_prefill_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v, float* out,
-                       int32_t L, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
-                       float scale, int32_t* status, const DeviceInfo& dev, cudaStream_t stream,
-                       std::string* err) {
+                       int32_t L, int32_t q_off, int64_t kv_stride, int32_t n_heads,
+                       int32_t n_kv_heads, int32_t head_dim, float scale, int32_t* status,
+                       const DeviceInfo& dev, cudaStream_t stream, std::string* err) {
   if (!(head_dim == 64 || head_dim == 96 || head_dim == 128)) {
     *err = "prefill head_dim must be 64, 96 or 128";
     return GLA_ERR_NOT_SUPPORTED;
@@ -618,18 +624,23 @@ int launch_prefill_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
     *err = "prefill shared memory layout does not fit";
     return GLA_ERR_NOT_SUPPORTED;
   }
-  if (((int64_t)n_heads * head_dim * 2) % 16 != 0 || ((int64_t)n_kv_heads * head_dim * 2) % 16)
-    {
-    *err = "prefill row widths must be multiples of 16 bytes";
+  const int64_t qw = (int64_t)n_heads * head_dim, kvw = (int64_t)n_kv_heads * head_dim;
+  if ((qw * 2) % 16 != 0 || (kv_stride * 2) % 16 != 0) {
+    *err = "prefill row strides must be multiples of 16 bytes";
     return GLA_ERR_ALIGNMENT;
   }
+  if (kv_stride < kvw || q_off < 0 || (int64_t)q_off + L > INT32_MAX) {
+    *err = "bad prefill key/value rows";
+    return GLA_ERR_INVALID_ARG;
+  }
   PrefillArgs a{};
-  if (!encode_f16_rows(&a.tq, q, (int64_t)n_heads * head_dim, L, err) ||
-      !encode_f16_rows(&a.tk, k, (int64_t)n_kv_heads * head_dim, L, err) ||
-      !encode_f16_rows(&a.tv, v, (int64_t)n_kv_heads * head_dim, L, err))
+  if (!encode_f16_rows(&a.tq, q, qw, L, qw, err) ||
+      !encode_f16_rows(&a.tk, k, kvw, (int64_t)q_off + L, kv_stride, err) ||
+      !encode_f16_rows(&a.tv, v, kvw, (int64_t)q_off + L, kv_stride, err))
     return GLA_ERR_INVALID_ARG;
   a.out = out;
   a.L = L;
+  a.q_off = q_off;
   a.n_heads = n_heads;
   a.kv_mul = n_heads / n_kv_heads;
   a.scale_log2 = scale * 1.4426950408889634f;

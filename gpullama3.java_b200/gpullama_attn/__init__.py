@@ -79,6 +79,10 @@ _SIGS = {
     "gla_rope_append_attention_f32": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32,
                                              _P, _I32, _I32, _F, _I32]),
     "gla_decode_f32kv_noalloc": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F, _P]),
+    "gla_ingest_prompt_f32": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
+                                     _I32, _F, _I32]),
+    "gla_ingest_prompt_f16kv": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
+                                       _I32, _F, _I32]),
 }
 
 EXPORTED_SYMBOLS = tuple(_SIGS)
@@ -304,6 +308,16 @@ class Context:
             self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(key_cache), _ptr(value_cache), _ptr(xb),
             n_heads, head_size, kv_dim, kv_mul, _ptr(position_holder), layer, context_length,
             theta, style), "gla_rope_append_attention_f32")
+
+    def ingest_prompt(self, q, k, v, key_cache, value_cache, xb, start_pos, n_rows, n_heads,
+                      n_kv_heads, head_dim, context_length, theta, style=ROPE_INTERLEAVED,
+                      f16_cache=False):
+        """gla_ingest_prompt_f32/_f16kv: RoPE, KV append and causal attention of
+        positions start_pos..start_pos+n_rows-1 of one layer."""
+        name = "gla_ingest_prompt_f16kv" if f16_cache else "gla_ingest_prompt_f32"
+        self._check(getattr(self._L, name)(
+            self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(key_cache), _ptr(value_cache), _ptr(xb),
+            start_pos, n_rows, n_heads, n_kv_heads, head_dim, context_length, theta, style), name)
 
     def rope_append(self, q, k, v, key_cache, value_cache, n_heads, n_kv_heads, head_dim,
                     position_holder, theta, style=ROPE_INTERLEAVED):

@@ -321,6 +321,38 @@ int32_t gla_prefill_causal_f16(gla_ctx* ctx, const uint16_t* q, const uint16_t* 
                                const uint16_t* v, float* out, int32_t L, int32_t n_heads,
                                int32_t n_kv_heads, int32_t head_dim, float scale);
 
+/* Batched prompt ingestion of one layer: positions start_pos..start_pos+n_rows-1
+ * at once.  The reference ingests a prompt one position at a time
+ * (inference/InferenceEngine.java:88-99 CPU, :309-327 GPU), each position running
+ * RoPE (InferenceCore.java:82-94 / :210-225), the KV append (:99-100) and the
+ * attention block (:105-144); this call does the three for all rows, given the
+ * rows of a batched QKV projection:
+ *   q  [n_rows][n_heads*head_dim], k and v [n_rows][kv_dim] FP32, read only (the
+ *      reference's in-place rotation of state.q/state.k is an intermediate that
+ *      nothing reads after the attention block);
+ *   key_cache/value_cache: the layer's [context_length][kv_dim] cache; rows
+ *      start_pos+i receive k rotated for position start_pos+i and v (FP32, or
+ *      FP16 for _f16kv), rows
+ *      0..start_pos-1 hold earlier chunks (a prompt may be ingested in chunks);
+ *   xb [n_rows][n_heads*head_dim] FP32: row i = attention of position start_pos+i
+ *      over cache rows 0..start_pos+i, scale 1/sqrt(head_dim).
+ * RoPE as gla_rope_append_f32 (same frequencies, same rounding: the cache rows
+ * equal those of n_rows single-position calls).  Attention runs on the tcgen05
+ * prefill kernel with FP16 operands (q, k, v rounded to FP16; FP32 softmax and
+ * accumulation): the FP16 error bound applies to both variants, and both give
+ * bit-identical xb.  head_dim 64, 96 or 128.  Uses a context workspace grown on
+ * first use (not during stream capture). */
+int32_t gla_ingest_prompt_f32(gla_ctx* ctx, const float* q, const float* k, const float* v,
+                              float* key_cache, float* value_cache, float* xb, int32_t start_pos,
+                              int32_t n_rows, int32_t n_heads, int32_t n_kv_heads,
+                              int32_t head_dim, int32_t context_length, float theta,
+                              int32_t rope_style);
+int32_t gla_ingest_prompt_f16kv(gla_ctx* ctx, const float* q, const float* k, const float* v,
+                                uint16_t* key_cache, uint16_t* value_cache, float* xb,
+                                int32_t start_pos, int32_t n_rows, int32_t n_heads,
+                                int32_t n_kv_heads, int32_t head_dim, int32_t context_length,
+                                float theta, int32_t rope_style);
+
 /* ------------------------------------------------------------------------ */
 /* Input producers: RoPE + KV append (the step before attention)             */
 /* ------------------------------------------------------------------------ */
