@@ -781,10 +781,43 @@ def run_e2e(args, ctx, wl, inp, torch, device, stream, dist):
 
     ms = timed(step_graph)
     ms_eager = timed(step_eager)
+
+    # the step after attention too: each layer's wo projection (FP16 [dim][dim],
+    # its own matrix per layer) with the residual add, gla_wo_residual_f16
+    # launched right behind the attention call (programmatic dependent launch)
+    dim = nh * hd
+    g16 = torch.Generator(device=device).manual_seed(6)
+    wo = [(torch.randn(dim, dim, device=device, generator=g16) * 0.02).half() for _ in range(L)]
+    x_res = torch.zeros(dim, device=device)
+
+    def layers_wo():
+        for l in range(L):
+            q = dev_in[l, : nh * hd]
+            k = dev_in[l, nh * hd: nh * hd + kvd]
+            v = dev_in[l, nh * hd + kvd:]
+            ctx.rope_append_attention(q, k, v, K, V, xb[l], nh, hd, kvd, nh // nkv, pos, l, T,
+                                      theta)
+            ctx.wo_residual(xb[l], x_res, wo[l], dim, dim)
+
+    with torch.cuda.stream(stream):
+        layers_wo()
+    torch.cuda.synchronize(device)
+    graph_wo = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_wo, stream=stream):
+        layers_wo()
+    torch.cuda.synchronize(device)
+
+    def step_graph_wo():
+        dev_in.copy_(host_in, non_blocking=True)
+        graph_wo.replay()
+        host_out.copy_(xb, non_blocking=True)
+
+    ms_wo = timed(step_graph_wo)
     st = ctx.device_status()
     if st != 0:
         raise RuntimeError(f"device status {st} in the e2e loop")
-    del graph
+    del graph, graph_wo
+    wo_bytes = L * dim * dim * 2 * world
     return {"value": round(bytes_step / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
             "ms_per_step": round(ms, 5),
             "h2d_bytes_per_step": int(host_in.numel() * 4),
@@ -795,6 +828,12 @@ def run_e2e(args, ctx, wl, inp, torch, device, stream, dist):
             "eager": {"value": round(bytes_step / (ms_eager * 1e-3) / 1e9, 2),
                       "ms_per_step": round(ms_eager, 5),
                       "path": "the same calls issued eagerly from Python every step"},
+            "with_wo": {"ms_per_step": round(ms_wo, 5),
+                        "us_per_layer": round(ms_wo * 1e3 / L, 3),
+                        "kv_plus_wo_GBps": round((bytes_step + wo_bytes) / (ms_wo * 1e-3) / 1e9,
+                                                 2),
+                        "path": "the graph above plus gla_wo_residual_f16 (FP16 wo, "
+                                f"{dim}x{dim}, residual add) after every layer's attention"},
             "gpu_launches_per_step": L}
 
 

@@ -725,6 +725,19 @@ int ingest_prompt(gla_ctx* ctx, bool f16_cache, const float* q, const float* k, 
 
 }  // namespace
 
+int32_t gla_wo_residual_f16(gla_ctx* ctx, const float* xb, float* x, const uint16_t* w, int32_t n,
+                            int32_t d) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  if (!xb || !x || !w) return fail(ctx, GLA_ERR_INVALID_ARG, "null pointer");
+  if (n < 8 || d < 1) return fail(ctx, GLA_ERR_INVALID_ARG, "bad wo shape");
+  if (n % 8 != 0 || !aligned16(w) || !aligned16(xb))
+    return fail(ctx, GLA_ERR_ALIGNMENT, "wo needs n % 8 == 0 and 16-byte aligned w and xb");
+  DeviceGuard dg(ctx->device);
+  std::string err;
+  int rc = gla::launch_wo_residual_f16(w, xb, x, n, d, ctx->dev, ctx->stream, &err);
+  return rc == GLA_OK ? GLA_OK : fail(ctx, rc, err);
+}
+
 int32_t gla_ingest_prompt_f32(gla_ctx* ctx, const float* q, const float* k, const float* v,
                               float* key_cache, float* value_cache, float* xb, int32_t start_pos,
                               int32_t n_rows, int32_t n_heads, int32_t n_kv_heads,

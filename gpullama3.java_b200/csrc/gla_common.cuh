@@ -8,6 +8,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+#include <atomic>
+
 #include "gpullama_attn.h"
 
 #define GLA_HD __host__ __device__ __forceinline__
@@ -414,5 +417,23 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 }
 
 #endif  // __CUDACC__
+
+// Raises the kernel's dynamic shared memory limit to the device's opt-in
+// maximum once per (kernel, device): the attribute is per function and
+// context, and setting it on every launch cost ~1 us of host time.
+template <class Kern>
+void ensure_smem_attr(Kern kern, size_t bytes, std::atomic<uint64_t>& done) {
+  // done: bit d set once device d has the attribute (devices < 64)
+  if (bytes <= 48 * 1024) return;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return;
+  int optin = 0;
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           std::max<int>(optin, (int)bytes)) == cudaSuccess && bit)
+    done.fetch_or(bit, std::memory_order_acq_rel);
+}
 
 }  // namespace gla

@@ -87,6 +87,10 @@ int launch_prefill_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
                        int32_t n_kv_heads, int32_t head_dim, float scale, int32_t* status,
                        const DeviceInfo& dev, cudaStream_t stream, std::string* err);
 
+// Output projection + residual (wo.cu): x[i] += w[i][:] . xb, w FP16 [d][n].
+int launch_wo_residual_f16(const uint16_t* w, const float* xb, float* x, int32_t n, int32_t d,
+                           const DeviceInfo& dev, cudaStream_t stream, std::string* err);
+
 // Batched prompt ingestion of one layer (ingest.cu): RoPE, KV append and
 // causal attention of n_rows positions from start_pos.  ws holds
 // ingest_workspace_halves(...) halves, 16-byte aligned.

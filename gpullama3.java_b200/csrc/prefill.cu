@@ -594,8 +594,8 @@ int launch_hd(PrefillArgs a, cudaStream_t stream, std::string* err) {
   const size_t smem = SM::kBytes + 1024;
   a.n_qblocks = (a.L + kBM * NT - 1) / (kBM * NT);
   const int grid = a.n_qblocks * a.n_heads;
-  cudaFuncSetAttribute(prefill_kernel<HD, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       (int)smem);
+  static std::atomic<uint64_t> smem_set{0};  // one per instantiation
+  ensure_smem_attr(prefill_kernel<HD, NT>, smem, smem_set);
   prefill_kernel<HD, NT><<<grid, SM::kThreads, smem, stream>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

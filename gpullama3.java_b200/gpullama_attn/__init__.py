@@ -79,6 +79,7 @@ _SIGS = {
     "gla_rope_append_attention_f32": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32,
                                              _P, _I32, _I32, _F, _I32]),
     "gla_decode_f32kv_noalloc": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F, _P]),
+    "gla_wo_residual_f16": (_I32, [_P, _P, _P, _P, _I32, _I32]),
     "gla_ingest_prompt_f32": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
                                      _I32, _F, _I32]),
     "gla_ingest_prompt_f16kv": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
@@ -308,6 +309,11 @@ class Context:
             self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(key_cache), _ptr(value_cache), _ptr(xb),
             n_heads, head_size, kv_dim, kv_mul, _ptr(position_holder), layer, context_length,
             theta, style), "gla_rope_append_attention_f32")
+
+    def wo_residual(self, xb, x, w, n, d):
+        """gla_wo_residual_f16: x += w . xb (w FP16 [d][n])."""
+        self._check(self._L.gla_wo_residual_f16(self._h, _ptr(xb), _ptr(x), _ptr(w), n, d),
+                    "gla_wo_residual_f16")
 
     def ingest_prompt(self, q, k, v, key_cache, value_cache, xb, start_pos, n_rows, n_heads,
                       n_kv_heads, head_dim, context_length, theta, style=ROPE_INTERLEAVED,

@@ -354,6 +354,24 @@ int32_t gla_ingest_prompt_f16kv(gla_ctx* ctx, const float* q, const float* k, co
                                 float theta, int32_t rope_style);
 
 /* ------------------------------------------------------------------------ */
+/* Output projection (the step after attention)                              */
+/* ------------------------------------------------------------------------ */
+
+/* x[i] = x[i] + sum_j w[i*n + j] * xb[j] for i in [0, d): the wo projection of
+ * the attention output with the residual add, the reference's GPU task
+ * "matmul1" = matrixVectorGenericWithResidual(context, xb, x, wo, n, d, 32)
+ * (tornadovm/kernels/TransformerComputeKernelsLayered.java:715-733,
+ * LlamaFP16FFNLayers.java:131; on the CPU InferenceCore.java:147-150).
+ * w FP16 [d][n] row-major (HalfFloatArray), xb [n] and x [d] FP32; FP32
+ * products and sums in a different order than the reference's 32-lane tree
+ * (results agree to FP32 rounding, not bit for bit).  n % 8 == 0, w and xb
+ * 16-byte aligned.  Launched with programmatic dependent launch: issued right
+ * after an attention call on the same stream, it streams the weights while
+ * the attention finishes and reads xb only once it has. */
+int32_t gla_wo_residual_f16(gla_ctx* ctx, const float* xb, float* x, const uint16_t* w, int32_t n,
+                            int32_t d);
+
+/* ------------------------------------------------------------------------ */
 /* Input producers: RoPE + KV append (the step before attention)             */
 /* ------------------------------------------------------------------------ */
 

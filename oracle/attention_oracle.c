@@ -29,6 +29,8 @@
  *   inference/InferenceCore.java:82-94      interleaved RoPE rotation (Llama)
  *   inference/InferenceCore.java:210-225    NeoX RoPE rotation (Qwen2; Qwen3 :351-366, Phi3 :473-487)
  *   inference/InferenceEngine.java:88-99    prompt ingestion = decode at 0..L-1
+ *   tornadovm/kernels/TransformerComputeKernelsLayered.java:715-733, :850-878
+ *                                           wo projection + residual (GPU task "matmul1")
  */
 #include <math.h>
 #include <stdint.h>
@@ -311,3 +313,28 @@ void oracle_rope_neox(float* q, float* k, int n_heads, int n_kv_heads, int head_
   }
 }
 
+
+/* matrixVectorGenericWithResidual (TransformerComputeKernelsLayered.java:715-733)
+ * through matrixVectorRowMajorOptimized's HalfFloatArray overload (:850-878):
+ * one workgroup of local_size threads per output row; thread t accumulates
+ * w[row*n + j] * x[j] for j = t, t + local_size, ... in that order, then the
+ * tree reduction localSum[t] += localSum[t + stride] for stride =
+ * local_size/2 .. 1, and hb[row] = hb[row] + localSum[0].  The GPU layer
+ * plan launches it with local_size 32 (LOCAL_WORK_GROUP_SIZE_ALLOC,
+ * tornadovm/layers/AbstractLayer.java:20; LlamaFP16FFNLayers.java:131). */
+void oracle_wo_residual_f16(const float* x, float* hb, const uint16_t* w, int n, int d,
+                            int local_size) {
+  float local_sum[1024];
+  if (local_size < 1 || local_size > 1024) return;
+  for (int row = 0; row < d; ++row) {
+    const uint16_t* wr = w + (int64_t)row * n;
+    for (int t = 0; t < local_size; ++t) {
+      float partial = 0.0f;
+      for (int j = t; j < n; j += local_size) partial += half_to_float(wr[j]) * x[j];
+      local_sum[t] = partial;
+    }
+    for (int stride = local_size / 2; stride > 0; stride >>= 1)
+      for (int t = 0; t < stride; ++t) local_sum[t] += local_sum[t + stride];
+    hb[row] = hb[row] + local_sum[0];
+  }
+}

@@ -56,6 +56,8 @@ def lib():
         L.oracle_rope_neox.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                        ctypes.c_int, _f32p, _f32p]
         L.oracle_half_to_float.argtypes = [_u16p, _f32p, ctypes.c_int64]
+        L.oracle_wo_residual_f16.argtypes = [_f32p, _f32p, _u16p, ctypes.c_int, ctypes.c_int,
+                                             ctypes.c_int]
         L.oracle_max_threads.restype = ctypes.c_int
         _lib = L
     return _lib
@@ -146,4 +148,14 @@ def half_to_float(h):
     h = np.ascontiguousarray(h).view(np.uint16)
     out = np.zeros(h.shape, dtype=np.float32)
     lib().oracle_half_to_float(_p(h, _u16p), _p(out), h.size)
+    return out
+
+
+def wo_residual_f16(x, hb, w16, n, d, local_size=32):
+    """x_res[i] += w[i]·xb as the GPU task matrixVectorGenericWithResidual does
+    it (TransformerComputeKernelsLayered.java:715-733): returns the new hb."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.array(hb, dtype=np.float32, copy=True)
+    w16 = np.ascontiguousarray(w16).view(np.uint16)
+    lib().oracle_wo_residual_f16(_p(x), _p(out), _p(w16, _u16p), n, d, local_size)
     return out
