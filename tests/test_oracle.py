@@ -141,3 +141,36 @@ def test_prefill_oracle_is_decode_per_row(oracle):
     for p in (0, 5, L - 1):
         xb = oracle.decode_f32(q[p], k, v, nh, nkv, hd, p + 1)
         np.testing.assert_array_equal(out[p], xb)
+
+
+def test_wo_residual_oracle_known_answers_and_float64(oracle):
+    """matrixVectorGenericWithResidual restatement: identity weights add xb to
+    the residual exactly; random weights agree with float64 to FP32 rounding;
+    the 32-lane tree order is what makes it differ from a plain loop."""
+    n = d = 64
+    eye = np.eye(d, n, dtype=np.float16)
+    xb = np.arange(n, dtype=np.float32) * 0.5
+    x = np.ones(d, dtype=np.float32)
+    np.testing.assert_array_equal(oracle.wo_residual_f16(xb, x, eye, n, d), x + xb)
+    rng = np.random.Generator(np.random.PCG64(9))
+    for n, d in ((3072, 40), (8, 3), (4104, 5)):
+        w = (rng.standard_normal((d, n), dtype=np.float32) * 0.05).astype(np.float16)
+        xb = rng.standard_normal(n, dtype=np.float32)
+        x = rng.standard_normal(d, dtype=np.float32)
+        got = oracle.wo_residual_f16(xb, x, w, n, d)
+        w64 = w.astype(np.float64)
+        exact = x + w64 @ xb.astype(np.float64)
+        scale = np.abs(x) + np.abs(w64) @ np.abs(xb.astype(np.float64))
+        assert (np.abs(got - exact) <= 4e-6 * scale).all()
+    # a one-lane workgroup is a plain sequential FP32 dot product per row
+    n, d = 40, 3
+    w = (rng.standard_normal((d, n), dtype=np.float32) * 0.05).astype(np.float16)
+    xb = rng.standard_normal(n, dtype=np.float32)
+    x = rng.standard_normal(d, dtype=np.float32)
+    plain = np.empty(d, dtype=np.float32)
+    for i in range(d):
+        acc = np.float32(0.0)
+        for j in range(n):
+            acc = np.float32(acc + np.float32(np.float32(w[i, j]) * xb[j]))
+        plain[i] = np.float32(x[i] + acc)
+    np.testing.assert_array_equal(oracle.wo_residual_f16(xb, x, w, n, d, local_size=1), plain)
