@@ -548,6 +548,57 @@ int32_t gla_decode_f16kv(gla_ctx* ctx, const float* q, const uint16_t* k, const 
                        n_pos, scale, 0);
 }
 
+int32_t gla_decode_q8kv(gla_ctx* ctx, const float* q, const int8_t* k, const int8_t* v,
+                        const uint16_t* scales, float* xb, int32_t n_heads, int32_t n_kv_heads,
+                        int32_t head_dim, int64_t kv_stride, int32_t n_pos, float scale) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  if (!q || !k || !v || !scales || !xb) return fail(ctx, GLA_ERR_INVALID_ARG, "null pointer");
+  if (n_pos < 1) return fail(ctx, GLA_ERR_INVALID_ARG, "n_pos must be >= 1");
+  if (!std::isfinite(scale)) return fail(ctx, GLA_ERR_INVALID_ARG, "scale must be finite");
+  int rc = check_decode_shape(ctx, n_heads, n_kv_heads, head_dim, kv_stride, 1);
+  if (rc != GLA_OK) return rc;
+  if (head_dim != 64 && head_dim != 128)
+    return fail(ctx, GLA_ERR_NOT_SUPPORTED, "Q8 cache: head_dim 64 or 128");
+  if (kv_stride % 16 != 0) return fail(ctx, GLA_ERR_ALIGNMENT, "Q8 kv_stride must be a multiple of 16");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(scales) || !aligned16(xb))
+    return fail(ctx, GLA_ERR_ALIGNMENT, "q, k, v, scales and xb must be 16-byte aligned");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, GLA_ERR_CUDA, "cudaSetDevice failed");
+  gla::DecodeRequest req{};
+  req.dtype = GLA_DTYPE_Q8;
+  req.q = q;
+  req.k = k;
+  req.v = v;
+  req.scales = scales;
+  req.kv_stride = kv_stride;
+  req.n_pos = n_pos;
+  req.n_pos_cap = n_pos;
+  req.max_n_pos = n_pos;
+  req.batch = 1;
+  req.n_heads = n_heads;
+  req.n_kv = n_kv_heads;
+  req.head_dim = head_dim;
+  req.scale = scale;
+  req.out = xb;
+  return run_decode(ctx, req);
+}
+
+int32_t gla_kv_quantize_q8(gla_ctx* ctx, const float* k, const float* v, int64_t src_stride,
+                           int32_t n_rows, int32_t n_kv_heads, int32_t head_dim, int8_t* kq,
+                           int8_t* vq, int64_t kv_stride, uint16_t* scales) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  if (!k || !v || !kq || !vq || !scales) return fail(ctx, GLA_ERR_INVALID_ARG, "null pointer");
+  if (n_rows < 1 || n_kv_heads < 1 || head_dim < 32 || head_dim > 128 || head_dim % 32 != 0)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "bad quantisation shape");
+  if (src_stride < (int64_t)n_kv_heads * head_dim || kv_stride < (int64_t)n_kv_heads * head_dim)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "row strides shorter than n_kv_heads * head_dim");
+  DeviceGuard dg(ctx->device);
+  std::string err;
+  int rc = gla::launch_quantize_q8(k, v, src_stride, n_rows, n_kv_heads, head_dim, kq, vq,
+                                   kv_stride, scales, ctx->stream, &err);
+  return rc == GLA_OK ? GLA_OK : fail(ctx, rc, err);
+}
+
 int32_t gla_decode_batched_f32kv(gla_ctx* ctx, const float* q, const float* const* k_ptrs,
                                  const float* const* v_ptrs, const int32_t* n_pos,
                                  int32_t max_n_pos, float* xb, int32_t batch, int32_t n_heads,

@@ -16,10 +16,11 @@ namespace gla {
 namespace {
 
 constexpr int kTileMax = 64;
-static_assert(F32Consumer<128, 1>::kTileMax == kTileMax && F16Consumer<128>::kTileMax == kTileMax,
+static_assert(F32Consumer<128, 1>::kTileMax == kTileMax && F16Consumer<128>::kTileMax == kTileMax &&
+                  Q8Consumer<128>::kTileMax == kTileMax,
               "consumers address stages with a compile-time tile height");
 
-// consumer warps: FP32 F32Consumer (8), FP16 F16Consumer (4)
+// consumer warps: FP32 F32Consumer (8), FP16 F16Consumer and Q8 Q8Consumer (4)
 int nw_for(int dtype) { return dtype == GLA_DTYPE_F32 ? 8 : 4; }
 constexpr int kMaxStages = 8;
 
@@ -29,10 +30,16 @@ size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 // LOADER 1 (cp.async) when the per-sequence bases live in device memory.
 int loader_for(const DecodeRequest& r) { return r.k_ptrs ? 1 : 0; }
 
-int esize_for(int dtype) { return dtype == GLA_DTYPE_F32 ? 4 : 2; }
+int esize_for(int dtype) { return dtype == GLA_DTYPE_F32 ? 4 : dtype == GLA_DTYPE_F16 ? 2 : 1; }
+
+// One stage: a K and a V tile, and for a Q8 cache the tile's scale rows.
+size_t stage_bytes_for(int dtype, int hd, int tile) {
+  return (size_t)2 * tile * hd * esize_for(dtype) +
+         (dtype == GLA_DTYPE_Q8 ? (size_t)tile * kQ8ScaleRowBytes : 0);
+}
 
 int group_cap_for(int dtype, int group) {
-  if (dtype == GLA_DTYPE_F16) return kMaxGroup;
+  if (dtype != GLA_DTYPE_F32) return kMaxGroup;
   return group <= 4 ? group : 8;
 }
 
@@ -44,7 +51,7 @@ struct Layout {
 
 Layout layout_for(int dtype, int hd, int group, int tile, int stages, int batch, int grid) {
   Layout L;
-  size_t off = (size_t)stages * 2 * tile * hd * esize_for(dtype);
+  size_t off = (size_t)stages * stage_bytes_for(dtype, hd, tile);
   L.off_bars = (int32_t)align16(off);
   off = L.off_bars + (size_t)stages * 2 * sizeof(uint64_t);
   L.off_seq = (int32_t)align16(off);
@@ -54,7 +61,7 @@ Layout layout_for(int dtype, int hd, int group, int tile, int stages, int batch,
   L.off_pbuf = (int32_t)align16(off);
   const int nw = nw_for(dtype);
   off = L.off_pbuf +
-        (dtype == GLA_DTYPE_F16 ? 0 : (size_t)nw * F32Consumer<128, 1>::kPbufFloats * sizeof(float));
+        (dtype != GLA_DTYPE_F32 ? 0 : (size_t)nw * F32Consumer<128, 1>::kPbufFloats * sizeof(float));
   L.off_merge = (int32_t)align16(off);
   off = L.off_merge + (size_t)nw * group_cap_for(dtype, group) * (hd + 4) * sizeof(float);
   L.off_flags = (int32_t)align16(off);
@@ -106,6 +113,13 @@ cudaError_t launch_any(int dtype, int hd, const DecodeArgs& a, const DecodePlan&
       default: return launch_f32<128, LOADER, XCH>(a, p, st);
     }
   }
+  if (dtype == GLA_DTYPE_Q8) {  // one sequence, tensor-map loader only (checked by the plan)
+    if constexpr (LOADER == 0 && !XCH) {
+      return hd == 64 ? launch_impl<64, Q8Consumer<64>, 0, false>(a, p, st)
+                      : launch_impl<128, Q8Consumer<128>, 0, false>(a, p, st);
+    }
+    return cudaErrorInvalidValue;
+  }
   switch (hd) {
     case 64: return launch_impl<64, F16Consumer<64>, LOADER, XCH>(a, p, st);
     case 96: return launch_impl<96, F16Consumer<96>, LOADER, XCH>(a, p, st);
@@ -139,20 +153,43 @@ bool encode_kv_map(CUtensorMap* map, const void* base, int dtype, int hd, int64_
     return false;
   }
   const int esize = esize_for(dtype);
-  const int cw = dtype == GLA_DTYPE_F32 ? 32 : (hd % 64 == 0 ? 64 : 32);
+  const int cw = dtype == GLA_DTYPE_F32 ? 32 : dtype == GLA_DTYPE_Q8 ? hd : (hd % 64 == 0 ? 64 : 32);
   const CUtensorMapSwizzle swz =
       cw * esize == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   cuuint64_t dims[2] = {(cuuint64_t)kv_stride, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(kv_stride * esize)};
   cuuint32_t box[2] = {(cuuint32_t)cw, (cuuint32_t)tile};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, dtype == GLA_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
-                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+  CUresult r = fn(map, dtype == GLA_DTYPE_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                      : dtype == GLA_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_UINT8,
                   2, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     *err = "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")";
+    return false;
+  }
+  return true;
+}
+
+// Q8 scales [rows][n_kv * 8] halves, boxes of one kv head's 8 halves x tile rows.
+bool encode_scale_map(CUtensorMap* map, const void* base, int n_kv, int64_t rows, int tile,
+                      std::string* err) {
+  auto fn = encode_fn();
+  if (!fn) {
+    *err = "cuTensorMapEncodeTiled unavailable";
+    return false;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)n_kv * kQ8ScaleHalves, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)n_kv * kQ8ScaleRowBytes};
+  cuuint32_t box[2] = {(cuuint32_t)kQ8ScaleHalves, (cuuint32_t)tile};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *err = "cuTensorMapEncodeTiled (scales) failed (" + std::to_string((int)r) + ")";
     return false;
   }
   return true;
@@ -173,6 +210,11 @@ int plan_decode(const DecodeRequest& r, const DeviceInfo& dev, DecodePlan* p, st
   }
   if (r.batch < 1 || r.batch > kMaxBatch) {
     *err = "batch must be in [1, 1024]";
+    return GLA_ERR_NOT_SUPPORTED;
+  }
+  if (r.dtype == GLA_DTYPE_Q8 &&
+      (!(hd == 64 || hd == 128) || r.k_ptrs || r.record_mode == 2 || r.rope || !r.scales)) {
+    *err = "Q8 cache: one sequence, head_dim 64 or 128";
     return GLA_ERR_NOT_SUPPORTED;
   }
   // Work is streamed and dealt to CTAs in whole tiles of kTileMax rows.
@@ -222,6 +264,9 @@ int launch_decode(const DecodeRequest& r, const DecodePlan& p, float* ws_part, i
     if (!encode_kv_map(&a.tmap_k, r.k, r.dtype, hd, r.kv_stride, r.n_pos_cap, p.tile, err) ||
         !encode_kv_map(&a.tmap_v, r.v, r.dtype, hd, r.kv_stride, r.n_pos_cap, p.tile, err))
       return GLA_ERR_INVALID_ARG;
+    if (r.dtype == GLA_DTYPE_Q8 &&
+        !encode_scale_map(&a.tmap_s, r.scales, r.n_kv, r.n_pos_cap, p.tile, err))
+      return GLA_ERR_INVALID_ARG;
   }
   a.q = r.q;
   a.k = r.k;
@@ -251,7 +296,7 @@ int launch_decode(const DecodeRequest& r, const DecodePlan& p, float* ws_part, i
   a.ws_part = ws_part;
   a.ws_counter = ws_counter;
   a.status = status;
-  a.stage_bytes = 2 * p.tile * hd * esize_for(r.dtype);
+  a.stage_bytes = (int32_t)stage_bytes_for(r.dtype, hd, p.tile);
   a.off_bars = L.off_bars;
   a.off_seq = L.off_seq;
   a.off_pbuf = L.off_pbuf;

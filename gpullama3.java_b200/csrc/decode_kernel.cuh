@@ -47,9 +47,15 @@
 
 namespace gla {
 
+// Q8 cache scales: one row of 8 halves per (key, kv head): the K block scales
+// (one per 32 values) at [0, HD/32), the V block scales at [4, 4 + HD/32).
+constexpr int kQ8ScaleHalves = 8;
+constexpr int kQ8ScaleRowBytes = 16;
+
 struct DecodeArgs {
   CUtensorMap tmap_k;          // LOADER 0: [rows][kv_stride] box (col_block, tile rows)
   CUtensorMap tmap_v;
+  CUtensorMap tmap_s;          // Q8 cache: scales [rows][n_kv * 8] halves, box (8, tile rows)
   const float* q;              // [B][n_heads][HD]
   const void* k;               // layer base (single sequence) or nullptr
   const void* v;
@@ -122,10 +128,13 @@ constexpr float kLn2 = 0.69314718055994530942f;
 // ---------------------------------------------------------------------------
 template <int ESIZE, int HD>
 struct TileLayout {
-  static constexpr int kCW = (ESIZE == 4) ? 32 : ((HD % 64 == 0) ? 64 : 32);
+  // FP32: 32-element blocks; FP16: 64 (32 for head_dim 96); int8: the whole
+  // head row (64 or 128 bytes)
+  static constexpr int kCW = (ESIZE == 4) ? 32 : (ESIZE == 2) ? ((HD % 64 == 0) ? 64 : 32) : HD;
   static constexpr int kRowB = kCW * ESIZE;  // 128 or 64
   static constexpr int kBlocks = HD / kCW;
   static_assert(HD % kCW == 0, "head_dim must be a multiple of the column block");
+  static_assert(kRowB == 128 || kRowB == 64, "tile rows are 64 or 128 bytes");
   // byte offset of the 16-byte chunk holding (row, col); col % (16/ESIZE) == 0
   __device__ __forceinline__ static int chunk_off(int tile, int row, int col) {
     const int cb = col / kCW;
@@ -159,6 +168,7 @@ template <int HD, int GT>
 struct F32Consumer {
   using TL = TileLayout<4, HD>;
   static constexpr int kElemBytes = 4;
+  static constexpr bool kQ8 = false;
   static constexpr int kNW = 8;
   static constexpr int kRows = 8;               // rows per warp
   static constexpr int kTileMax = kRows * kNW;  // 64: the only tile height plans use
@@ -407,6 +417,7 @@ template <int HD>
 struct F16Consumer {
   using TL = TileLayout<2, HD>;
   static constexpr int kElemBytes = 2;
+  static constexpr bool kQ8 = false;
   static constexpr int kNW = 4;
   static constexpr int kPbufFloats = 0;
   static constexpr int kTileMax = 16 * kNW;
@@ -544,6 +555,207 @@ struct F16Consumer {
       for (int nt = 0; nt < kNT; ++nt)
         *reinterpret_cast<float2*>(mh + nt * 8 + 2 * tig) =
             make_float2(oacc[nt][0] + oacc[nt][2], oacc[nt][1] + oacc[nt][3]);
+      if (tig == 0) *reinterpret_cast<float2*>(mh + HD) = make_float2(m_run, lt);
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Q8 cache consumer: int8 K/V values with one FP16 scale per 32 values of a
+// head row (Q8_0-style blocks; the scales of a key sit side by side, see
+// kQ8ScaleHalves).  The warp layout and the hi/lo MMA scheme are
+// F16Consumer's.  int8 values become FP16 exactly (|v| <= 128: the byte,
+// offset by 128, is placed in the mantissa of 1024.0 and 1152 subtracted);
+// the scales are applied in FP32: each 32-column block of q.k is multiplied
+// by its key's K scale, and p is multiplied by its key's V scale of an output
+// block before the hi/lo split.  ldmatrix reads int8 pairs as 16-bit elements:
+//   q.k: the head_dim columns are permuted inside every 16-column step
+//     (k index 2t+e <-> column 4t+e, 8+2t+e <-> 4t+2+e, for q and K alike,
+//     which leaves the dot product unchanged), so the four bytes a lane gets
+//     from a plain ldmatrix are its two B registers;
+//   p.v: a transposed ldmatrix gives a lane keys (2t, 2t+1) x columns
+//     (2j, 2j+1): bytes 0 and 2 are its B register for column 2j, bytes 1
+//     and 3 for column 2j+1, so a 16-column block is two n-tiles (even and
+//     odd columns) and a lane's outputs land on 4 consecutive columns.
+// Keys past n_pos: scores -inf and p exactly 0 (their scale bytes may be
+// anything), int8 values are finite.
+// ---------------------------------------------------------------------------
+// Two of r's signed bytes (chosen by sel, a prmt selector placing them in
+// the low bytes of the halves) as an exact half2.
+__device__ __forceinline__ uint32_t i8pair_to_h2(uint32_t r, uint32_t sel) {
+  uint32_t h;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(h) : "r"(r ^ 0x80808080u), "r"(0x64646464u), "r"(sel));
+  const __half2 x = __hsub2(*reinterpret_cast<const __half2*>(&h), __half2half2(__ushort_as_half(0x6480)));
+  return *reinterpret_cast<const uint32_t*>(&x);
+}
+constexpr uint32_t kSelB01 = 0x4140u, kSelB23 = 0x4342u, kSelB02 = 0x4240u, kSelB13 = 0x4341u;
+
+template <int HD>
+struct Q8Consumer {
+  using TL = TileLayout<1, HD>;
+  static constexpr int kElemBytes = 1;
+  static constexpr bool kQ8 = true;
+  static constexpr int kNW = 4;
+  static constexpr int kPbufFloats = 0;
+  static constexpr int kTileMax = 16 * kNW;
+  static constexpr int kMergeG = kMaxGroup;
+  static constexpr int kKS = HD / 16;  // k-steps of q.k
+  static constexpr int kNB = HD / 32;  // scale blocks of a head row
+  static constexpr int kNT = HD / 8;   // n-tiles of p.v
+  static_assert(HD == 64 || HD == 128, "Q8 cache: head_dim 64 or 128");
+
+  uint32_t qa[kKS][4];
+  float m_run, l_run;
+  float oacc[kNT][4];
+
+  __device__ __forceinline__ static uint32_t chunk(uint32_t base, int tile, int row, int col) {
+    return base + (uint32_t)TL::chunk_off(tile, row, col);
+  }
+
+  __device__ __forceinline__ void begin(const DecodeArgs&, const float* qs, int lane) {
+    const int gid = lane >> 2, tig = lane & 3;
+    const float* qh = qs + gid * HD;
+#pragma unroll
+    for (int kk = 0; kk < kKS; ++kk) {
+      // permuted columns: k (2t, 2t+1) <- 4t, 4t+1; k (2t+8, 2t+9) <- 4t+2, 4t+3
+      const float4 u = *reinterpret_cast<const float4*>(qh + kk * 16 + 4 * tig);
+      __half h0, l0, h1, l1, h2, l2, h3, l3;
+      split_half(u.x, h0, l0); split_half(u.y, h1, l1);
+      split_half(u.z, h2, l2); split_half(u.w, h3, l3);
+      qa[kk][0] = pack_half2(h0, h1);
+      qa[kk][1] = pack_half2(l0, l1);
+      qa[kk][2] = pack_half2(h2, h3);
+      qa[kk][3] = pack_half2(l2, l3);
+    }
+    m_run = -INFINITY;
+    l_run = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < kNT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) oacc[nt][e] = 0.f;
+  }
+
+  __device__ __forceinline__ void consume(const DecodeArgs& a, const char* stage, int rows,
+                                          float* /*pbuf_w*/, const float* /*qs*/, int w,
+                                          int lane) {
+    const int rb = w * 16;
+    if (rb >= rows) return;
+    const int nvalid = min(16, rows - rb);
+    const int tig = lane & 3, mi = lane >> 3;
+    const uint32_t kbase = smem_u32(stage);
+    const uint32_t vbase = kbase + (uint32_t)(a.tile * HD);
+    const char* sbase = stage + (size_t)2 * a.tile * HD;
+    // the block scales of the lane's 4 keys rb + nt*8 + 2*tig + e
+    uint4 sc[2][2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e)
+        sc[nt][e] = *reinterpret_cast<const uint4*>(sbase + (rb + nt * 8 + 2 * tig + e) *
+                                                                kQ8ScaleRowBytes);
+    auto scale_of = [&](int nt, int e, int idx) {  // idx: 0..3 K blocks, 4..7 V blocks
+      const uint4 v4 = sc[nt][e];
+      const uint32_t word = (idx >> 1) == 0 ? v4.x : (idx >> 1) == 1 ? v4.y
+                            : (idx >> 1) == 2 ? v4.z : v4.w;
+      return __half2float(
+          __ushort_as_half((unsigned short)((idx & 1) ? (word >> 16) : (word & 0xffffu))));
+    };
+    float s[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+#pragma unroll
+    for (int b = 0; b < kNB; ++b) {
+      float tmp[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) tmp[nt][e] = 0.f;
+      // matrices: keys 0-7 / 8-15 of the warp's rows x steps 2b / 2b+1
+      uint32_t r0, r1, r2, r3;
+      ldsm_x4(chunk(kbase, a.tile, rb + (mi & 1) * 8 + (lane & 7), (2 * b + (mi >> 1)) * 16), r0,
+              r1, r2, r3);
+      mma_16816(tmp[0], qa[2 * b], i8pair_to_h2(r0, kSelB01), i8pair_to_h2(r0, kSelB23));
+      mma_16816(tmp[1], qa[2 * b], i8pair_to_h2(r1, kSelB01), i8pair_to_h2(r1, kSelB23));
+      mma_16816(tmp[0], qa[2 * b + 1], i8pair_to_h2(r2, kSelB01), i8pair_to_h2(r2, kSelB23));
+      mma_16816(tmp[1], qa[2 * b + 1], i8pair_to_h2(r3, kSelB01), i8pair_to_h2(r3, kSelB23));
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+          s[nt][e] = fmaf(tmp[nt][e] + tmp[nt][2 + e], scale_of(nt, e, b), s[nt][e]);
+    }
+    float mt = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int pos = nt * 8 + 2 * tig + e;
+        s[nt][e] = pos < nvalid ? s[nt][e] : -INFINITY;
+        mt = fmaxf(mt, s[nt][e]);
+      }
+    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+    const float mn = fmaxf(m_run, mt);  // finite: row rb is valid
+    const float alpha = fast_exp2(m_run - mn);
+    float p[2][2];
+    float psum = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        p[nt][e] = fast_exp2(s[nt][e] - mn);
+        psum += p[nt][e];
+      }
+    l_run = l_run * alpha + psum;
+    m_run = mn;
+#pragma unroll
+    for (int nt = 0; nt < kNT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) oacc[nt][e] *= alpha;
+#pragma unroll
+    for (int b = 0; b < kNB; ++b) {
+      // p times the key's V scale of output block b (exactly 0 past n_pos)
+      uint32_t pa[4];
+      {
+        float pv[2][2];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e)
+            pv[nt][e] = (nt * 8 + 2 * tig + e < nvalid) ? p[nt][e] * scale_of(nt, e, 4 + b) : 0.f;
+        __half h00, l00, h01, l01, h10, l10, h11, l11;
+        split_half(pv[0][0], h00, l00); split_half(pv[0][1], h01, l01);
+        split_half(pv[1][0], h10, l10); split_half(pv[1][1], h11, l11);
+        pa[0] = pack_half2(h00, h01);
+        pa[1] = pack_half2(l00, l01);
+        pa[2] = pack_half2(h10, h11);
+        pa[3] = pack_half2(l10, l11);
+      }
+      // matrices: keys 0-7 / 8-15 x columns 32b..32b+15 / 32b+16..32b+31
+      uint32_t r0, r1, r2, r3;
+      ldsm_x4_t(chunk(vbase, a.tile, rb + (mi & 1) * 8 + (lane & 7), 32 * b + (mi >> 1) * 16), r0,
+                r1, r2, r3);
+      mma_16816(oacc[4 * b + 0], pa, i8pair_to_h2(r0, kSelB02), i8pair_to_h2(r1, kSelB02));
+      mma_16816(oacc[4 * b + 1], pa, i8pair_to_h2(r0, kSelB13), i8pair_to_h2(r1, kSelB13));
+      mma_16816(oacc[4 * b + 2], pa, i8pair_to_h2(r2, kSelB02), i8pair_to_h2(r3, kSelB02));
+      mma_16816(oacc[4 * b + 3], pa, i8pair_to_h2(r2, kSelB13), i8pair_to_h2(r3, kSelB13));
+    }
+  }
+
+  __device__ __forceinline__ void to_merge(const DecodeArgs& a, float* merge_w, int lane) {
+    const int gid = lane >> 2, tig = lane & 3;
+    float lt = l_run;
+    lt += __shfl_xor_sync(0xffffffffu, lt, 1);
+    lt += __shfl_xor_sync(0xffffffffu, lt, 2);
+    if (gid < a.group) {
+      float* mh = merge_w + gid * merge_head_floats<HD>();
+      // n-tiles 2c (even columns) and 2c+1 (odd) of 16-column block c: this
+      // lane's columns 16c + 4*tig .. +3
+#pragma unroll
+      for (int c = 0; c < HD / 16; ++c) {
+        const float (&ev)[4] = oacc[2 * c];
+        const float (&od)[4] = oacc[2 * c + 1];
+        *reinterpret_cast<float4*>(mh + 16 * c + 4 * tig) =
+            make_float4(ev[0] + ev[2], od[0] + od[2], ev[1] + ev[3], od[1] + od[3]);
+      }
       if (tig == 0) *reinterpret_cast<float2*>(mh + HD) = make_float2(m_run, lt);
     }
   }
@@ -716,6 +928,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   // fence orders those generic stores before the tensor copy that reads the
   // row back (only the CTA holding that row's tile does this).
   auto append_row = [&](int g) {
+    if constexpr (Consumer::kElemBytes != 4) return;  // fused RoPE writes FP32 caches only
     const int pos = npos[0] - 1;
     float* kc = const_cast<float*>(static_cast<const float*>(a.k)) + (int64_t)pos * a.kv_stride +
                 (int64_t)g * HD;
@@ -743,7 +956,8 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
   auto tma_tile = [&](int st, const Tile& t, uint64_t pol) {
     char* ks = smem + (size_t)st * a.stage_bytes;
     char* vs = ks + (size_t)a.tile * HD * esize;
-    mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * a.tile * HD * esize));
+    mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * a.tile * HD * esize +
+                                                (Consumer::kQ8 ? a.tile * kQ8ScaleRowBytes : 0)));
 #pragma unroll
     for (int cb = 0; cb < TL::kBlocks; ++cb) {
       const int x = t.g * HD + cb * TL::kCW;
@@ -751,6 +965,10 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
       tma_load_2d(ks + off, &a.tmap_k, x, t.row0, &full[st], pol);
       tma_load_2d(vs + off, &a.tmap_v, x, t.row0, &full[st], pol);
     }
+    // Q8 cache: the K and V block scales of kv head g, one 16-byte row a key
+    if constexpr (Consumer::kQ8)
+      tma_load_2d(ks + (size_t)2 * a.tile * HD, &a.tmap_s, t.g * kQ8ScaleHalves, t.row0,
+                  &full[st], pol);
   };
   // Early KV prefetch (programmatic dependent launch).  The work partition
   // needs only the positions, so the producer may start streaming this CTA's

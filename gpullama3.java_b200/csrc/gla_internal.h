@@ -11,10 +11,11 @@ namespace gla {
 
 // Everything a decode launch needs besides pointers checked by the caller.
 struct DecodeRequest {
-  int dtype;                   // GLA_DTYPE_F32 / GLA_DTYPE_F16
+  int dtype;                   // GLA_DTYPE_F32 / GLA_DTYPE_F16 / GLA_DTYPE_Q8
   const float* q;
   const void* k;
   const void* v;
+  const void* scales = nullptr;  // Q8: [rows][n_kv][8] halves (K, V block scales)
   const void* const* k_ptrs;
   const void* const* v_ptrs;
   int64_t kv_stride;
@@ -86,6 +87,11 @@ int launch_prefill_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
                        int32_t L, int32_t q_off, int64_t kv_stride, int32_t n_heads,
                        int32_t n_kv_heads, int32_t head_dim, float scale, int32_t* status,
                        const DeviceInfo& dev, cudaStream_t stream, std::string* err);
+
+// Q8 cache rows from FP32 K/V rows (q8.cu); scales [rows][n_kv][8] halves.
+int launch_quantize_q8(const float* k, const float* v, int64_t src_stride, int32_t n_rows,
+                       int32_t n_kv, int32_t hd, int8_t* kq, int8_t* vq, int64_t kv_stride,
+                       uint16_t* scales, cudaStream_t stream, std::string* err);
 
 // Output projection + residual (wo.cu): x[i] += w[i][:] . xb, w FP16 [d][n].
 int launch_wo_residual_f16(const uint16_t* w, const float* xb, float* x, int32_t n, int32_t d,

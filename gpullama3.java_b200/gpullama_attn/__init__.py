@@ -80,6 +80,8 @@ _SIGS = {
                                              _P, _I32, _I32, _F, _I32]),
     "gla_decode_f32kv_noalloc": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F, _P]),
     "gla_wo_residual_f16": (_I32, [_P, _P, _P, _P, _I32, _I32]),
+    "gla_decode_q8kv": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F]),
+    "gla_kv_quantize_q8": (_I32, [_P, _P, _P, _I64, _I32, _I32, _I32, _P, _P, _I64, _P]),
     "gla_ingest_prompt_f32": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
                                      _I32, _F, _I32]),
     "gla_ingest_prompt_f16kv": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
@@ -309,6 +311,28 @@ class Context:
             self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(key_cache), _ptr(value_cache), _ptr(xb),
             n_heads, head_size, kv_dim, kv_mul, _ptr(position_holder), layer, context_length,
             theta, style), "gla_rope_append_attention_f32")
+
+    def decode_q8(self, q, k, v, scales, xb, n_heads, n_kv_heads, head_dim, n_pos,
+                  kv_stride=None, scale=None):
+        """gla_decode_q8kv: decode over a Q8 cache (int8 k/v, FP16 block scales)."""
+        if kv_stride is None:
+            kv_stride = n_kv_heads * head_dim
+        if scale is None:
+            scale = 1.0 / math.sqrt(head_dim)
+        self._check(self._L.gla_decode_q8kv(self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(scales),
+                                            _ptr(xb), n_heads, n_kv_heads, head_dim, kv_stride,
+                                            n_pos, scale), "gla_decode_q8kv")
+
+    def quantize_q8(self, k, v, n_rows, n_kv_heads, head_dim, kq, vq, scales, src_stride=None,
+                    kv_stride=None):
+        """gla_kv_quantize_q8: FP32 K/V rows into Q8 cache rows."""
+        if src_stride is None:
+            src_stride = n_kv_heads * head_dim
+        if kv_stride is None:
+            kv_stride = n_kv_heads * head_dim
+        self._check(self._L.gla_kv_quantize_q8(self._h, _ptr(k), _ptr(v), src_stride, n_rows,
+                                               n_kv_heads, head_dim, _ptr(kq), _ptr(vq),
+                                               kv_stride, _ptr(scales)), "gla_kv_quantize_q8")
 
     def wo_residual(self, xb, x, w, n, d):
         """gla_wo_residual_f16: x += w . xb (w FP16 [d][n])."""

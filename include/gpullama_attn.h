@@ -47,6 +47,7 @@ extern "C" {
 /* element types */
 #define GLA_DTYPE_F32 0
 #define GLA_DTYPE_F16 1
+#define GLA_DTYPE_Q8 2 /* int8 values + FP16 scale per 32 (see gla_decode_q8kv) */
 
 typedef struct gla_ctx gla_ctx;
 
@@ -203,6 +204,27 @@ int32_t gla_decode_f32kv(gla_ctx* ctx, const float* q, const float* k, const flo
 int32_t gla_decode_f16kv(gla_ctx* ctx, const float* q, const uint16_t* k, const uint16_t* v,
                          float* xb, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                          int64_t kv_stride, int32_t n_pos, float scale);
+
+/* Q8 cache (an addition: the reference's caches are FP32; the block shape is
+ * that of its quantised weight type Q8_0, tensor/GGMLType.java:13):
+ *   k, v    int8 [n_pos][kv_stride] (kv head g at column g*head_dim),
+ *   scales  FP16 bits [n_pos][n_kv_heads][8]: the K scales of the head row's
+ *           32-value blocks at [0, head_dim/32), the V scales at [4, ...);
+ * element = q * (float)scale.  Attention is computed on those values with FP32
+ * accuracy (int8 values and hi/lo-split q and p on FP16 tensor cores, scales
+ * applied in FP32).  head_dim 64 or 128; kv_stride a multiple of 16; k, v,
+ * scales, q, xb 16-byte aligned.  Half the bytes of an FP16 cache. */
+int32_t gla_decode_q8kv(gla_ctx* ctx, const float* q, const int8_t* k, const int8_t* v,
+                        const uint16_t* scales, float* xb, int32_t n_heads, int32_t n_kv_heads,
+                        int32_t head_dim, int64_t kv_stride, int32_t n_pos, float scale);
+
+/* Quantises n_rows FP32 rows of K and V ([n_rows][src_stride], n_kv_heads heads of
+ * head_dim) into Q8 cache rows: per 32-value block d = amax/127, q = roundf(x/d)
+ * computed as x * (1/d), d stored as FP16 (GGML's Q8_0 reference quantiser).
+ * kq/vq/scales point at the first destination row. */
+int32_t gla_kv_quantize_q8(gla_ctx* ctx, const float* k, const float* v, int64_t src_stride,
+                           int32_t n_rows, int32_t n_kv_heads, int32_t head_dim, int8_t* kq,
+                           int8_t* vq, int64_t kv_stride, uint16_t* scales);
 
 /* Batched decode: `batch` independent sequences, one new token each.
  *  q  [batch][n_heads][head_dim], xb [batch][n_heads][head_dim]

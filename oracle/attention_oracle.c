@@ -31,6 +31,8 @@
  *   inference/InferenceEngine.java:88-99    prompt ingestion = decode at 0..L-1
  *   tornadovm/kernels/TransformerComputeKernelsLayered.java:715-733, :850-878
  *                                           wo projection + residual (GPU task "matmul1")
+ *   tensor/GGMLType.java:13 (Q8_0 block shape) and GGML's published Q8_0 reference
+ *   quantiser (ggml, quantize_row_q8_0_ref)  Q8 KV cache quantisation
  */
 #include <math.h>
 #include <stdint.h>
@@ -337,4 +339,60 @@ void oracle_wo_residual_f16(const float* x, float* hb, const uint16_t* w, int n,
       for (int t = 0; t < stride; ++t) local_sum[t] += local_sum[t + stride];
     hb[row] = hb[row] + local_sum[0];
   }
+}
+
+/* IEEE binary32 -> binary16, round to nearest even (NaN -> quiet NaN). */
+static uint16_t float_to_half_rne(float f) {
+  uint32_t x;
+  memcpy(&x, &f, 4);
+  const uint16_t sign = (uint16_t)((x >> 16) & 0x8000u);
+  const uint32_t a = x & 0x7fffffffu;
+  if (a >= 0x7f800000u) return sign | (a > 0x7f800000u ? 0x7e00u : 0x7c00u);
+  if (a >= 0x477ff000u) return sign | 0x7c00u; /* >= 65520 rounds to infinity */
+  if (a < 0x38800000u) {                       /* below 2^-14: subnormal half */
+    float af;
+    memcpy(&af, &a, 4);
+    return sign | (uint16_t)nearbyint((double)af * 16777216.0); /* units of 2^-24 */
+  }
+  uint32_t h = ((((a >> 23) - 127 + 15) & 0x1fu) << 10) | ((a & 0x7fffffu) >> 13);
+  const uint32_t rem = a & 0x1fffu;
+  if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) ++h; /* a carry may raise the exponent */
+  return sign | (uint16_t)h;
+}
+
+void oracle_float_to_half(const float* in, uint16_t* out, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) out[i] = float_to_half_rne(in[i]);
+}
+
+/* Q8 KV cache rows as GGML's Q8_0 reference quantiser does a block of 32:
+ * amax = max |x|, d = amax / 127, id = d ? 1/d : 0, q = roundf(x * id), d kept
+ * as FP16.  Layout: values [rows][kv_stride] int8 (head g at g*hd), scales
+ * [rows][n_kv][8] FP16 bits with K blocks at 0.. and V blocks at 4.., the other
+ * halves 0. */
+static void quantize_head_row(const float* x, int8_t* q, uint16_t* s, int nb) {
+  for (int b = 0; b < nb; ++b) {
+    float amax = 0.0f;
+    for (int j = 0; j < 32; ++j) {
+      const float ax = fabsf(x[32 * b + j]);
+      if (ax > amax) amax = ax;
+    }
+    const float d = amax / 127.0f;
+    const float id = d != 0.0f ? 1.0f / d : 0.0f;
+    for (int j = 0; j < 32; ++j) q[32 * b + j] = (int8_t)roundf(x[32 * b + j] * id);
+    s[b] = float_to_half_rne(d);
+  }
+}
+
+void oracle_quantize_q8(const float* k, const float* v, int64_t src_stride, int n_rows, int n_kv,
+                        int hd, int8_t* kq, int8_t* vq, int64_t kv_stride, uint16_t* scales) {
+  const int nb = hd / 32;
+  for (int64_t r = 0; r < n_rows; ++r)
+    for (int g = 0; g < n_kv; ++g) {
+      uint16_t* srow = scales + (r * n_kv + g) * 8;
+      memset(srow, 0, 8 * sizeof(uint16_t));
+      quantize_head_row(k + r * src_stride + (int64_t)g * hd, kq + r * kv_stride + (int64_t)g * hd,
+                        srow, nb);
+      quantize_head_row(v + r * src_stride + (int64_t)g * hd, vq + r * kv_stride + (int64_t)g * hd,
+                        srow + 4, nb);
+    }
 }

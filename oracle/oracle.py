@@ -58,6 +58,10 @@ def lib():
         L.oracle_half_to_float.argtypes = [_u16p, _f32p, ctypes.c_int64]
         L.oracle_wo_residual_f16.argtypes = [_f32p, _f32p, _u16p, ctypes.c_int, ctypes.c_int,
                                              ctypes.c_int]
+        _i8p = ctypes.POINTER(ctypes.c_int8)
+        L.oracle_float_to_half.argtypes = [_f32p, _u16p, ctypes.c_int64]
+        L.oracle_quantize_q8.argtypes = [_f32p, _f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_int, _i8p, _i8p, ctypes.c_int64, _u16p]
         L.oracle_max_threads.restype = ctypes.c_int
         _lib = L
     return _lib
@@ -159,3 +163,37 @@ def wo_residual_f16(x, hb, w16, n, d, local_size=32):
     w16 = np.ascontiguousarray(w16).view(np.uint16)
     lib().oracle_wo_residual_f16(_p(x), _p(out), _p(w16, _u16p), n, d, local_size)
     return out
+
+
+def float_to_half(x):
+    """IEEE float32 -> float16 bits, round to nearest even."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.zeros(x.shape, dtype=np.uint16)
+    lib().oracle_float_to_half(_p(x), _p(out, _u16p), x.size)
+    return out
+
+
+def quantize_q8(k, v, n_kv, hd):
+    """Q8 KV cache rows of FP32 k/v [rows][n_kv*hd] (GGML Q8_0 quantiser):
+    returns (kq int8, vq int8, scales uint16 [rows][n_kv][8])."""
+    k = np.ascontiguousarray(k, dtype=np.float32)
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    rows = k.shape[0]
+    kq = np.zeros((rows, n_kv * hd), dtype=np.int8)
+    vq = np.zeros_like(kq)
+    sc = np.zeros((rows, n_kv, 8), dtype=np.uint16)
+    i8 = ctypes.POINTER(ctypes.c_int8)
+    lib().oracle_quantize_q8(_p(k), _p(v), n_kv * hd, rows, n_kv, hd, _p(kq, i8), _p(vq, i8),
+                             n_kv * hd, _p(sc, _u16p))
+    return kq, vq, sc
+
+
+def dequantize_q8(kq, vq, sc, n_kv, hd):
+    """FP32 values q * scale of a Q8 cache (exact in FP32)."""
+    rows = kq.shape[0]
+    nb = hd // 32
+    s = half_to_float(sc).reshape(rows, n_kv, 8)
+    ks = np.repeat(s[:, :, :nb], 32, axis=2).reshape(rows, n_kv * hd)
+    vs = np.repeat(s[:, :, 4:4 + nb], 32, axis=2).reshape(rows, n_kv * hd)
+    return (kq.astype(np.float32) * ks).astype(np.float32), \
+        (vq.astype(np.float32) * vs).astype(np.float32)

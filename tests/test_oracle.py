@@ -174,3 +174,36 @@ def test_wo_residual_oracle_known_answers_and_float64(oracle):
             acc = np.float32(acc + np.float32(np.float32(w[i, j]) * xb[j]))
         plain[i] = np.float32(x[i] + acc)
     np.testing.assert_array_equal(oracle.wo_residual_f16(xb, x, w, n, d, local_size=1), plain)
+
+
+def test_float_to_half_and_q8_quantiser(oracle):
+    """The oracle's FP16 rounding equals numpy's (round to nearest even, edge
+    cases included), and its Q8_0 quantiser equals a numpy restatement of
+    GGML's: d = amax/127, q = round-half-away(x * (1/d)), d stored as FP16;
+    dequantised values are within half a step of the input."""
+    rng = np.random.Generator(np.random.PCG64(4))
+    x = np.concatenate([rng.standard_normal(20000, dtype=np.float32) * s
+                        for s in (1e-8, 1e-5, 1e-3, 1.0, 1e2, 1e4, 6e4)])
+    x = np.concatenate([x, np.array([65504, 65519.99, 65520, -65520, 5.96e-8, 2.98e-8, 2.99e-8,
+                                     0.0, -0.0, np.inf, -np.inf], dtype=np.float32)])
+    with np.errstate(over="ignore"):
+        np.testing.assert_array_equal(oracle.float_to_half(x), x.astype(np.float16).view(np.uint16))
+    n_kv, hd, rows = 3, 128, 40
+    k = rng.standard_normal((rows, n_kv * hd), dtype=np.float32) * 2
+    v = rng.standard_normal((rows, n_kv * hd), dtype=np.float32)
+    k[0, :32] = 0.0
+    kq, vq, sc = oracle.quantize_q8(k, v, n_kv, hd)
+    for src, q, lo in ((k, kq, 0), (v, vq, 4)):
+        b = src.reshape(rows, n_kv, 4, 32)
+        amax = np.abs(b).max(axis=3)
+        d = (amax / np.float32(127)).astype(np.float32)
+        inv = np.where(d != 0, np.float32(1) / np.where(d != 0, d, 1), 0).astype(np.float32)
+        y = (b * inv[..., None]).astype(np.float32)
+        qn = np.where(y >= 0, np.floor(y + 0.5), -np.floor(-y + 0.5)).astype(np.int8)
+        np.testing.assert_array_equal(q.reshape(rows, n_kv, 4, 32), qn)
+        np.testing.assert_array_equal(sc[:, :, lo:lo + 4], d.astype(np.float16).view(np.uint16))
+    assert (sc[0, 0, 0] == 0) and (kq[0, :32] == 0).all()
+    kd, vd = oracle.dequantize_q8(kq, vq, sc, n_kv, hd)
+    step = oracle.half_to_float(sc[:, :, :4]).repeat(32, axis=2).reshape(rows, n_kv * hd)
+    # half a step, plus 127 times the FP16 rounding of the step (<= 2^-11 of it)
+    assert (np.abs(kd - k) <= (0.5 + 127 * 2.0 ** -11) * step * (1 + 1e-6) + 1e-30).all()
