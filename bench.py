@@ -54,6 +54,10 @@ WORKLOADS = {
                T=131072, f16=True, theta=None, batch=1),
     "c5": dict(name="phi3-mini-causal-prefill-attn", layers=1, n_heads=32, n_kv=32, hd=96,
                T=4096, f16=True, theta=None, batch=1),
+    # not a BASELINE config: config 4's shape over a Q8 cache (int8 values, an
+    # FP16 scale per 32), one replica per GPU
+    "c4q8": dict(name="qwen2.5-7b-longctx-decode-attn-q8kv", layers=1, n_heads=28, n_kv=4, hd=128,
+                 T=131072, f16=False, theta=None, batch=1),
 }
 
 FALLBACK_HBM_GBS = 6650.0
@@ -837,6 +841,133 @@ def run_e2e(args, ctx, wl, inp, torch, device, stream, dist):
             "gpu_launches_per_step": L}
 
 
+def run_q8(args, rank, world, local_rank, dist):
+    """Config 4's shape (Qwen2.5-7B: 28 heads, 4 kv heads, hd 128, 131072
+    positions) over a Q8 cache: int8 K/V values and FP16 block scales
+    (gla_kv_quantize_q8 fills it from seeded FP32 rows), one gla_decode_q8kv a
+    step, one replica per GPU.  KV bytes a step: 2*T*kv_dim + T*n_kv*16
+    (142.6 MB, above the 126 MB L2, so the cache streams from HBM)."""
+    import torch
+    import gpullama_attn as gla
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    wl = WORKLOADS["c4q8"]
+    nh, nkv, hd, T = wl["n_heads"], wl["n_kv"], wl["hd"], wl["T"]
+    kvd = nkv * hd
+    stream = torch.cuda.Stream(device)
+    ctx = gla.Context(local_rank, stream.cuda_stream)
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    with torch.cuda.stream(stream):
+        kq = torch.empty(T, kvd, dtype=torch.int8, device=device)
+        vq = torch.empty_like(kq)
+        sc = torch.empty(T, nkv, 8, dtype=torch.int16, device=device)
+        chunk = 16384
+        for r0 in range(0, T, chunk):
+            n = min(chunk, T - r0)
+            kf = torch.randn(n, kvd, device=device, generator=g)
+            vf = torch.randn(n, kvd, device=device, generator=g)
+            ctx.quantize_q8(kf, vf, n, nkv, hd, kq[r0:], vq[r0:], sc[r0:])
+        q = torch.randn(nh * hd, device=device, generator=g)
+        xb = torch.empty(nh * hd, device=device)
+    torch.cuda.synchronize(device)
+    del kf, vf
+
+    def step():
+        ctx.decode_q8(q, kq, vq, sc, xb, nh, nkv, hd, T)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    torch.cuda.synchronize(device)
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    t_soak = time.perf_counter()
+    per = max(ms_est(graph.replay, stream, torch, device), 1e-3)
+    soak = 0 if args.quick else int(min(20000, 1000.0 / per))
+    if dist is not None:
+        t = torch.tensor([soak], device=device, dtype=torch.int64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        soak = int(t.item())
+    with torch.cuda.stream(stream):
+        for _ in range(soak):
+            graph.replay()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    soak_s = time.perf_counter() - t_soak
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / args.steps
+    clocks = sampler.stop() if sampler else None
+    if dist is not None:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if ctx.device_status() != 0:
+        raise RuntimeError("device status after the timed region")
+    # e2e: q from pinned host memory, the call, xb back (the cache stays resident)
+    hq = q.cpu().pin_memory()
+    hx = torch.empty(nh * hd).pin_memory()
+
+    def e2e_step():
+        q.copy_(hq, non_blocking=True)
+        step()
+        hx.copy_(xb, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize(device)
+        w0 = time.perf_counter()
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = max(e0.elapsed_time(e1), (time.perf_counter() - w0) * 1e3) / args.steps
+    del graph
+    kv_bytes = 2 * T * kvd + T * nkv * 16
+    peak, peak_kind = peaks()
+    gbs = kv_bytes * world / (ms * 1e-3) / 1e9
+    res = {
+        "metric": "decode-attn KV-read GB/s", "value": round(gbs, 2), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 5), "us_per_layer_step": round(ms * 1e3, 3),
+        "tokens_per_s_equiv": round(1e3 / ms, 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "q8 (int8 + f16 block scales), f32 acc",
+        "data": "synthetic ~N(0,1) rows quantised on the device, seeded torch generator",
+        "config": {"workload": wl["name"], "baseline_config": "c4 shape, Q8 cache (extra)",
+                   "n_heads": nh, "n_kv_heads": nkv, "head_dim": hd, "context": T,
+                   "kv_dtype": "q8", "kv_bytes_per_step_per_gpu": kv_bytes,
+                   "l2": "142.6 MB cache > 126 MB L2, no flush",
+                   "parallelism": f"replicas{world}" if world > 1 else "single"},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(kv_bytes / (ms * 1e-3) / 1e9, 1),
+                     "peak": peak, "unit": "GB/s",
+                     "frac": round(kv_bytes / (ms * 1e-3) / 1e9 / peak, 4), "traffic": None,
+                     "peak_source": peak_kind, "kernel": "gla::decode_kernel<Q8Consumer<128>>",
+                     "bytes_per_launch": kv_bytes},
+        "clocks": dict(clocks, soak_s=round(soak_s, 2)) if clocks else None,
+        "e2e": {"value": round(kv_bytes * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": int(hq.numel() * 4),
+                "d2h_bytes_per_step": int(hx.numel() * 4)},
+    }
+    ctx.close()
+    return res
+
+
 # ---------------------------------------------------------------------------
 # Reference arm: the reference's CPU attention (C restatement) on host cores
 # ---------------------------------------------------------------------------
@@ -874,6 +1005,9 @@ def run_reference(args, rank, world):
     wl = WORKLOADS[args.workload]
     if args.workload == "c5":
         return run_reference_prefill(args, world)
+    if args.workload == "c4q8":
+        return {"impl": "reference",
+                "unavailable": "the reference keeps FP32 KV caches: it has no Q8 cache path"}
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import oracle  # the reference's CPU path, restated
 
@@ -976,6 +1110,8 @@ def main():
     try:
         if args.workload == "c5":
             res = run_prefill(args, rank, world, local_rank, dist)
+        elif args.workload == "c4q8":
+            res = run_q8(args, rank, world, local_rank, dist)
         else:
             res = run_ours(args, rank, world, local_rank, dist)
         if rank == 0:

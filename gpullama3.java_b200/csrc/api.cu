@@ -384,6 +384,8 @@ int32_t gla_create(int32_t device, void* cuda_stream, gla_ctx** out) {
   }
   cudaDeviceGetAttribute(&ctx->dev.sms, cudaDevAttrMultiProcessorCount, device);
   cudaDeviceGetAttribute(&ctx->dev.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  cudaDeviceGetAttribute(&ctx->dev.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor,
+                         device);
   if (cudaMalloc(&ctx->status, 256) != cudaSuccess) {
     delete ctx;
     return GLA_ERR_OUT_OF_MEMORY;

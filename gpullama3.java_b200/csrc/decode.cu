@@ -228,18 +228,27 @@ int plan_decode(const DecodeRequest& r, const DeviceInfo& dev, DecodePlan* p, st
     *err = "decode work too large for one call";
     return GLA_ERR_NOT_SUPPORTED;
   }
+  // The FP16 consumer with the cp.async loader (batches) runs two CTAs an SM
+  // (F16Consumer::kCtasPerSm), each with half an SM's shared memory.
+  const int per_sm = (r.dtype == GLA_DTYPE_F16 && loader_for(r) == 1 && r.record_mode != 2 &&
+                      dev.smem_per_sm > 0)
+                         ? 2
+                         : 1;
+  const size_t smem_cap =
+      per_sm == 1 ? (size_t)dev.smem_optin
+                  : std::min<size_t>(dev.smem_optin, (size_t)dev.smem_per_sm / 2 - 1024);
   // Every CTA participates when n_pos is only known on the device.
-  int grid = dev.sms;
-  if (r.n_pos_dev == nullptr) grid = (int)std::min<int64_t>(dev.sms, W);
+  int grid = dev.sms * per_sm;
+  if (r.n_pos_dev == nullptr) grid = (int)std::min<int64_t>(grid, W);
   grid = std::max(grid, 1);
   // Stages: as many as fit (the ring is the only large smem consumer).
   int stages = kMaxStages;
   Layout L = layout_for(r.dtype, hd, group, tile, stages, r.batch, grid);
-  while (stages > 2 && L.total > (size_t)dev.smem_optin) {
+  while (stages > 2 && L.total > smem_cap) {
     --stages;
     L = layout_for(r.dtype, hd, group, tile, stages, r.batch, grid);
   }
-  if (L.total > (size_t)dev.smem_optin) {
+  if (L.total > smem_cap) {
     *err = "shared memory layout does not fit";
     return GLA_ERR_NOT_SUPPORTED;
   }

@@ -169,6 +169,7 @@ struct F32Consumer {
   using TL = TileLayout<4, HD>;
   static constexpr int kElemBytes = 4;
   static constexpr bool kQ8 = false;
+  static constexpr int kCtasPerSm = 1;  // 8 consumer warps: one CTA fills the schedulers
   static constexpr int kNW = 8;
   static constexpr int kRows = 8;               // rows per warp
   static constexpr int kTileMax = kRows * kNW;  // 64: the only tile height plans use
@@ -418,6 +419,10 @@ struct F16Consumer {
   using TL = TileLayout<2, HD>;
   static constexpr int kElemBytes = 2;
   static constexpr bool kQ8 = false;
+  // with the cp.async loader (batches) two CTAs an SM: the producer warp's
+  // per-chunk copies limit one CTA (C3: 86 % of HBM against 70 %); the TMA
+  // loader keeps one CTA with the deeper ring (C4: 77 % against 70 %)
+  static constexpr int kCtasPerSm = 2;
   static constexpr int kNW = 4;
   static constexpr int kPbufFloats = 0;
   static constexpr int kTileMax = 16 * kNW;
@@ -580,11 +585,12 @@ struct F16Consumer {
 // Keys past n_pos: scores -inf and p exactly 0 (their scale bytes may be
 // anything), int8 values are finite.
 // ---------------------------------------------------------------------------
-// Two of r's signed bytes (chosen by sel, a prmt selector placing them in
-// the low bytes of the halves) as an exact half2.
-__device__ __forceinline__ uint32_t i8pair_to_h2(uint32_t r, uint32_t sel) {
+// Two bytes of u (chosen by sel, a prmt selector placing them in the low
+// bytes of the halves) as an exact half2; u holds signed int8 values offset
+// by 128 (r ^ 0x80808080).
+__device__ __forceinline__ uint32_t i8pair_to_h2(uint32_t u, uint32_t sel) {
   uint32_t h;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(h) : "r"(r ^ 0x80808080u), "r"(0x64646464u), "r"(sel));
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(h) : "r"(u), "r"(0x64646464u), "r"(sel));
   const __half2 x = __hsub2(*reinterpret_cast<const __half2*>(&h), __half2half2(__ushort_as_half(0x6480)));
   return *reinterpret_cast<const uint32_t*>(&x);
 }
@@ -595,6 +601,7 @@ struct Q8Consumer {
   using TL = TileLayout<1, HD>;
   static constexpr int kElemBytes = 1;
   static constexpr bool kQ8 = true;
+  static constexpr int kCtasPerSm = 1;  // TMA loader only
   static constexpr int kNW = 4;
   static constexpr int kPbufFloats = 0;
   static constexpr int kTileMax = 16 * kNW;
@@ -672,6 +679,10 @@ struct Q8Consumer {
       uint32_t r0, r1, r2, r3;
       ldsm_x4(chunk(kbase, a.tile, rb + (mi & 1) * 8 + (lane & 7), (2 * b + (mi >> 1)) * 16), r0,
               r1, r2, r3);
+      r0 ^= 0x80808080u;
+      r1 ^= 0x80808080u;
+      r2 ^= 0x80808080u;
+      r3 ^= 0x80808080u;
       mma_16816(tmp[0], qa[2 * b], i8pair_to_h2(r0, kSelB01), i8pair_to_h2(r0, kSelB23));
       mma_16816(tmp[1], qa[2 * b], i8pair_to_h2(r1, kSelB01), i8pair_to_h2(r1, kSelB23));
       mma_16816(tmp[0], qa[2 * b + 1], i8pair_to_h2(r2, kSelB01), i8pair_to_h2(r2, kSelB23));
@@ -733,6 +744,10 @@ struct Q8Consumer {
       uint32_t r0, r1, r2, r3;
       ldsm_x4_t(chunk(vbase, a.tile, rb + (mi & 1) * 8 + (lane & 7), 32 * b + (mi >> 1) * 16), r0,
                 r1, r2, r3);
+      r0 ^= 0x80808080u;
+      r1 ^= 0x80808080u;
+      r2 ^= 0x80808080u;
+      r3 ^= 0x80808080u;
       mma_16816(oacc[4 * b + 0], pa, i8pair_to_h2(r0, kSelB02), i8pair_to_h2(r1, kSelB02));
       mma_16816(oacc[4 * b + 1], pa, i8pair_to_h2(r0, kSelB13), i8pair_to_h2(r1, kSelB13));
       mma_16816(oacc[4 * b + 2], pa, i8pair_to_h2(r2, kSelB02), i8pair_to_h2(r3, kSelB02));
@@ -842,7 +857,8 @@ __device__ __forceinline__ void write_final4(const DecodeArgs& a, int b, int hq,
 // The kernel
 // ---------------------------------------------------------------------------
 template <int HD, class Consumer, int LOADER, bool XCH>
-__global__ void __launch_bounds__((Consumer::kNW + 1) * 32, 1)
+__global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
+                                  (LOADER == 1 && !XCH) ? Consumer::kCtasPerSm : 1)
     decode_kernel(const __grid_constant__ DecodeArgs a) {
   extern __shared__ __align__(1024) char smem_raw[];
   // swizzled TMA tiles need 1024-byte aligned stages (the host adds the slack)

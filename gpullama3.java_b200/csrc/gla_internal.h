@@ -61,6 +61,7 @@ struct DecodePlan {
 struct DeviceInfo {
   int sms;
   int smem_optin;              // max dynamic shared memory per block
+  int smem_per_sm = 0;         // shared memory of an SM (0: plan one CTA an SM)
 };
 
 // Fills `plan` for `req`; returns GLA_OK or an error code with *err set.
