@@ -956,7 +956,8 @@ def run_q8(args, rank, world, local_rank, dist):
         "gpu_launches": args.steps,
         "roofline": {"bound": "hbm", "achieved": round(kv_bytes / (ms * 1e-3) / 1e9, 1),
                      "peak": peak, "unit": "GB/s",
-                     "frac": round(kv_bytes / (ms * 1e-3) / 1e9 / peak, 4), "traffic": None,
+                     "frac": round(kv_bytes / (ms * 1e-3) / 1e9 / peak, 4),
+                     "traffic": traffic_from_profiles("c4q8"),
                      "peak_source": peak_kind, "kernel": "gla::decode_kernel<Q8Consumer<128>>",
                      "bytes_per_launch": kv_bytes},
         "clocks": dict(clocks, soak_s=round(soak_s, 2)) if clocks else None,
@@ -1082,7 +1083,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true",
                     help="profiling runs: no clock soak, no e2e loop, no CPU baseline")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="profiling runs: fewer layers than the workload's (same per-layer "
+                         "launch), to keep an ncu capture small")
     args = ap.parse_args()
+    if args.layers is not None:
+        for wl in WORKLOADS.values():
+            wl["layers"] = max(1, min(wl["layers"], args.layers))
     if args.warmup < 3:
         args.warmup = 3  # timing rule: at least 3 warm-up steps
 
