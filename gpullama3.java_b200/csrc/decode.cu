@@ -20,8 +20,8 @@ static_assert(F32Consumer<128, 1>::kTileMax == kTileMax && F16Consumer<128>::kTi
                   Q8Consumer<128>::kTileMax == kTileMax,
               "consumers address stages with a compile-time tile height");
 
-// consumer warps: FP32 F32Consumer (8), FP16 F16Consumer and Q8 Q8Consumer (4)
-int nw_for(int dtype) { return dtype == GLA_DTYPE_F32 ? 8 : 4; }
+// consumer warps: F32Consumer (8), F16Consumer (4), Q8Consumer (8)
+int nw_for(int dtype) { return dtype == GLA_DTYPE_F16 ? 4 : 8; }
 constexpr int kMaxStages = 8;
 
 size_t align16(size_t x) { return (x + 15) & ~size_t(15); }

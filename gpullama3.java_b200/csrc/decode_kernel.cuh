@@ -568,8 +568,8 @@ struct F16Consumer {
 // ---------------------------------------------------------------------------
 // Q8 cache consumer: int8 K/V values with one FP16 scale per 32 values of a
 // head row (Q8_0-style blocks; the scales of a key sit side by side, see
-// kQ8ScaleHalves).  The warp layout and the hi/lo MMA scheme are
-// F16Consumer's.  int8 values become FP16 exactly (|v| <= 128: the byte,
+// kQ8ScaleHalves).  The hi/lo MMA scheme is F16Consumer's.  int8 values
+// become FP16 exactly (|v| <= 128: the byte,
 // offset by 128, is placed in the mantissa of 1024.0 and 1152 subtracted);
 // the scales are applied in FP32: each 32-column block of q.k is multiplied
 // by its key's K scale, and p is multiplied by its key's V scale of an output
@@ -580,7 +580,7 @@ struct F16Consumer {
 //     from a plain ldmatrix are its two B registers;
 //   p.v: a transposed ldmatrix gives a lane keys (2t, 2t+1) x columns
 //     (2j, 2j+1): bytes 0 and 2 are its B register for column 2j, bytes 1
-//     and 3 for column 2j+1, so a 16-column block is two n-tiles (even and
+//     and 3 for column 2j+1, so a 16-column group is two n-tiles (even and
 //     odd columns) and a lane's outputs land on 4 consecutive columns.
 // Keys past n_pos: scores -inf and p exactly 0 (their scale bytes may be
 // anything), int8 values are finite.
@@ -596,15 +596,38 @@ __device__ __forceinline__ uint32_t i8pair_to_h2(uint32_t u, uint32_t sel) {
 }
 constexpr uint32_t kSelB01 = 0x4140u, kSelB23 = 0x4342u, kSelB02 = 0x4240u, kSelB13 = 0x4341u;
 
+__device__ __forceinline__ void mma_1688(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(b0));
+}
+
+// (x0, x1) as hi and lo half2 pairs: hi = half(x), lo = half(x - float(hi)).
+__device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(x0, x1);
+  const float2 hf = __half22float2(h);
+  const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// 8 consumer warps, each owning 8 keys of a 64-row tile (two warps a
+// scheduler: the per-warp chain is latency-bound).  q.k: m16n8k16, one
+// ldmatrix.x4 covers the warp's 8 keys x 64 columns; p.v: m16n8k8 over the 8
+// keys, one transposed ldmatrix.x4 covers 8 keys x 64 columns (8 n-tiles).
+// O is rescaled only when a head's running max moved in this tile.
 template <int HD>
 struct Q8Consumer {
   using TL = TileLayout<1, HD>;
   static constexpr int kElemBytes = 1;
   static constexpr bool kQ8 = true;
   static constexpr int kCtasPerSm = 1;  // TMA loader only
-  static constexpr int kNW = 4;
+  static constexpr int kNW = 8;
+  static constexpr int kKeys = 8;       // keys of a tile per warp
   static constexpr int kPbufFloats = 0;
-  static constexpr int kTileMax = 16 * kNW;
+  static constexpr int kTileMax = kKeys * kNW;
   static constexpr int kMergeG = kMaxGroup;
   static constexpr int kKS = HD / 16;  // k-steps of q.k
   static constexpr int kNB = HD / 32;  // scale blocks of a head row
@@ -626,13 +649,8 @@ struct Q8Consumer {
     for (int kk = 0; kk < kKS; ++kk) {
       // permuted columns: k (2t, 2t+1) <- 4t, 4t+1; k (2t+8, 2t+9) <- 4t+2, 4t+3
       const float4 u = *reinterpret_cast<const float4*>(qh + kk * 16 + 4 * tig);
-      __half h0, l0, h1, l1, h2, l2, h3, l3;
-      split_half(u.x, h0, l0); split_half(u.y, h1, l1);
-      split_half(u.z, h2, l2); split_half(u.w, h3, l3);
-      qa[kk][0] = pack_half2(h0, h1);
-      qa[kk][1] = pack_half2(l0, l1);
-      qa[kk][2] = pack_half2(h2, h3);
-      qa[kk][3] = pack_half2(l2, l3);
+      split2(u.x, u.y, qa[kk][0], qa[kk][1]);
+      split2(u.z, u.w, qa[kk][2], qa[kk][3]);
     }
     m_run = -INFINITY;
     l_run = 0.f;
@@ -645,113 +663,89 @@ struct Q8Consumer {
   __device__ __forceinline__ void consume(const DecodeArgs& a, const char* stage, int rows,
                                           float* /*pbuf_w*/, const float* /*qs*/, int w,
                                           int lane) {
-    const int rb = w * 16;
+    const int rb = w * kKeys;
     if (rb >= rows) return;
-    const int nvalid = min(16, rows - rb);
+    const int nvalid = min(kKeys, rows - rb);
     const int tig = lane & 3, mi = lane >> 3;
     const uint32_t kbase = smem_u32(stage);
     const uint32_t vbase = kbase + (uint32_t)(a.tile * HD);
     const char* sbase = stage + (size_t)2 * a.tile * HD;
-    // the block scales of the lane's 4 keys rb + nt*8 + 2*tig + e
-    uint4 sc[2][2];
+    // the block scales of the lane's keys rb + 2*tig + e: halves 0..3 K, 4..7 V
+    uint4 sc[2];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e)
-        sc[nt][e] = *reinterpret_cast<const uint4*>(sbase + (rb + nt * 8 + 2 * tig + e) *
-                                                                kQ8ScaleRowBytes);
-    auto scale_of = [&](int nt, int e, int idx) {  // idx: 0..3 K blocks, 4..7 V blocks
-      const uint4 v4 = sc[nt][e];
-      const uint32_t word = (idx >> 1) == 0 ? v4.x : (idx >> 1) == 1 ? v4.y
-                            : (idx >> 1) == 2 ? v4.z : v4.w;
+    for (int e = 0; e < 2; ++e)
+      sc[e] = *reinterpret_cast<const uint4*>(sbase + (rb + 2 * tig + e) * kQ8ScaleRowBytes);
+    auto scale_of = [&](int e, int idx) {
+      const uint32_t word = (idx >> 1) == 0 ? sc[e].x : (idx >> 1) == 1 ? sc[e].y
+                            : (idx >> 1) == 2 ? sc[e].z : sc[e].w;
       return __half2float(
           __ushort_as_half((unsigned short)((idx & 1) ? (word >> 16) : (word & 0xffffu))));
     };
-    float s[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    // ---- scores: per 32-column block, q.k times the key's K scale
+    float s[2] = {0.f, 0.f};
 #pragma unroll
-    for (int b = 0; b < kNB; ++b) {
-      float tmp[2][4];
+    for (int q4 = 0; q4 < kKS / 4; ++q4) {
+      uint32_t r[4];  // matrix j: the warp's 8 keys x k-step 4*q4 + j
+      ldsm_x4(chunk(kbase, a.tile, rb + (lane & 7), (4 * q4 + mi) * 16), r[0], r[1], r[2], r[3]);
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
+      for (int j = 0; j < 4; ++j) r[j] ^= 0x80808080u;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) tmp[nt][e] = 0.f;
-      // matrices: keys 0-7 / 8-15 of the warp's rows x steps 2b / 2b+1
-      uint32_t r0, r1, r2, r3;
-      ldsm_x4(chunk(kbase, a.tile, rb + (mi & 1) * 8 + (lane & 7), (2 * b + (mi >> 1)) * 16), r0,
-              r1, r2, r3);
-      r0 ^= 0x80808080u;
-      r1 ^= 0x80808080u;
-      r2 ^= 0x80808080u;
-      r3 ^= 0x80808080u;
-      mma_16816(tmp[0], qa[2 * b], i8pair_to_h2(r0, kSelB01), i8pair_to_h2(r0, kSelB23));
-      mma_16816(tmp[1], qa[2 * b], i8pair_to_h2(r1, kSelB01), i8pair_to_h2(r1, kSelB23));
-      mma_16816(tmp[0], qa[2 * b + 1], i8pair_to_h2(r2, kSelB01), i8pair_to_h2(r2, kSelB23));
-      mma_16816(tmp[1], qa[2 * b + 1], i8pair_to_h2(r3, kSelB01), i8pair_to_h2(r3, kSelB23));
+      for (int hb = 0; hb < 2; ++hb) {
+        const int b = 2 * q4 + hb;
+        float tmp[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_16816(tmp, qa[2 * b], i8pair_to_h2(r[2 * hb], kSelB01),
+                  i8pair_to_h2(r[2 * hb], kSelB23));
+        mma_16816(tmp, qa[2 * b + 1], i8pair_to_h2(r[2 * hb + 1], kSelB01),
+                  i8pair_to_h2(r[2 * hb + 1], kSelB23));
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e)
-          s[nt][e] = fmaf(tmp[nt][e] + tmp[nt][2 + e], scale_of(nt, e, b), s[nt][e]);
+        for (int e = 0; e < 2; ++e) s[e] = fmaf(tmp[e] + tmp[2 + e], scale_of(e, b), s[e]);
+      }
     }
+    // ---- online softmax over the warp's 8 keys
     float mt = -INFINITY;
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int pos = nt * 8 + 2 * tig + e;
-        s[nt][e] = pos < nvalid ? s[nt][e] : -INFINITY;
-        mt = fmaxf(mt, s[nt][e]);
-      }
+    for (int e = 0; e < 2; ++e) {
+      s[e] = 2 * tig + e < nvalid ? s[e] : -INFINITY;
+      mt = fmaxf(mt, s[e]);
+    }
     mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
     mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
-    const float mn = fmaxf(m_run, mt);  // finite: row rb is valid
+    const float mn = fmaxf(m_run, mt);  // finite: key rb is valid
     const float alpha = fast_exp2(m_run - mn);
-    float p[2][2];
-    float psum = 0.f;
+    float p[2];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
+    for (int e = 0; e < 2; ++e) p[e] = fast_exp2(s[e] - mn);
+    l_run = l_run * alpha + (p[0] + p[1]);
+    if (__any_sync(0xffffffffu, mn != m_run)) {
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        p[nt][e] = fast_exp2(s[nt][e] - mn);
-        psum += p[nt][e];
-      }
-    l_run = l_run * alpha + psum;
+      for (int nt = 0; nt < kNT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) oacc[nt][e] *= alpha;
+    }
     m_run = mn;
+    // ---- p.v: per output block, p times the key's V scale (0 past n_pos)
 #pragma unroll
-    for (int nt = 0; nt < kNT; ++nt)
+    for (int q4 = 0; q4 < HD / 64; ++q4) {
+      uint32_t r[4];  // matrix j: the warp's 8 keys x columns 64*q4 + 16*j .. +15
+      ldsm_x4_t(chunk(vbase, a.tile, rb + (lane & 7), 64 * q4 + 16 * mi), r[0], r[1], r[2], r[3]);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) oacc[nt][e] *= alpha;
+      for (int j = 0; j < 4; ++j) r[j] ^= 0x80808080u;
 #pragma unroll
-    for (int b = 0; b < kNB; ++b) {
-      // p times the key's V scale of output block b (exactly 0 past n_pos)
-      uint32_t pa[4];
-      {
-        float pv[2][2];
+      for (int hb = 0; hb < 2; ++hb) {
+        const int b = 2 * q4 + hb;
+        float pv[2];
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
+        for (int e = 0; e < 2; ++e) pv[e] = 2 * tig + e < nvalid ? p[e] * scale_of(e, 4 + b) : 0.f;
+        uint32_t ahi, alo;
+        split2(pv[0], pv[1], ahi, alo);
 #pragma unroll
-          for (int e = 0; e < 2; ++e)
-            pv[nt][e] = (nt * 8 + 2 * tig + e < nvalid) ? p[nt][e] * scale_of(nt, e, 4 + b) : 0.f;
-        __half h00, l00, h01, l01, h10, l10, h11, l11;
-        split_half(pv[0][0], h00, l00); split_half(pv[0][1], h01, l01);
-        split_half(pv[1][0], h10, l10); split_half(pv[1][1], h11, l11);
-        pa[0] = pack_half2(h00, h01);
-        pa[1] = pack_half2(l00, l01);
-        pa[2] = pack_half2(h10, h11);
-        pa[3] = pack_half2(l10, l11);
+        for (int jj = 0; jj < 2; ++jj) {
+          const int j = 2 * hb + jj;
+          const int c = 4 * q4 + j;  // 16-column group: n-tiles 2c (even), 2c+1 (odd)
+          mma_1688(oacc[2 * c], ahi, alo, i8pair_to_h2(r[j], kSelB02));
+          mma_1688(oacc[2 * c + 1], ahi, alo, i8pair_to_h2(r[j], kSelB13));
+        }
       }
-      // matrices: keys 0-7 / 8-15 x columns 32b..32b+15 / 32b+16..32b+31
-      uint32_t r0, r1, r2, r3;
-      ldsm_x4_t(chunk(vbase, a.tile, rb + (mi & 1) * 8 + (lane & 7), 32 * b + (mi >> 1) * 16), r0,
-                r1, r2, r3);
-      r0 ^= 0x80808080u;
-      r1 ^= 0x80808080u;
-      r2 ^= 0x80808080u;
-      r3 ^= 0x80808080u;
-      mma_16816(oacc[4 * b + 0], pa, i8pair_to_h2(r0, kSelB02), i8pair_to_h2(r1, kSelB02));
-      mma_16816(oacc[4 * b + 1], pa, i8pair_to_h2(r0, kSelB13), i8pair_to_h2(r1, kSelB13));
-      mma_16816(oacc[4 * b + 2], pa, i8pair_to_h2(r2, kSelB02), i8pair_to_h2(r3, kSelB02));
-      mma_16816(oacc[4 * b + 3], pa, i8pair_to_h2(r2, kSelB13), i8pair_to_h2(r3, kSelB13));
     }
   }
 
@@ -762,12 +756,12 @@ struct Q8Consumer {
     lt += __shfl_xor_sync(0xffffffffu, lt, 2);
     if (gid < a.group) {
       float* mh = merge_w + gid * merge_head_floats<HD>();
-      // n-tiles 2c (even columns) and 2c+1 (odd) of 16-column block c: this
+      // n-tiles 2c (even columns) and 2c+1 (odd) of 16-column group c: this
       // lane's columns 16c + 4*tig .. +3
 #pragma unroll
       for (int c = 0; c < HD / 16; ++c) {
-        const float (&ev)[4] = oacc[2 * c];
-        const float (&od)[4] = oacc[2 * c + 1];
+        const float(&ev)[4] = oacc[2 * c];
+        const float(&od)[4] = oacc[2 * c + 1];
         *reinterpret_cast<float4*>(mh + 16 * c + 4 * tig) =
             make_float4(ev[0] + ev[2], od[0] + od[2], ev[1] + ev[3], od[1] + od[3]);
       }
