@@ -601,6 +601,70 @@ int32_t gla_kv_quantize_q8(gla_ctx* ctx, const float* k, const float* v, int64_t
   return rc == GLA_OK ? GLA_OK : fail(ctx, rc, err);
 }
 
+int32_t gla_kv_cache_alloc_q8(gla_ctx* ctx, int32_t n_layers, int32_t context_length,
+                              int32_t n_kv_heads, int32_t head_dim, int8_t** key_cache,
+                              int8_t** value_cache, uint16_t** scales) {
+  if (!ctx || !key_cache || !value_cache || !scales) return GLA_ERR_INVALID_ARG;
+  *key_cache = *value_cache = nullptr;
+  *scales = nullptr;
+  if (n_layers < 1 || context_length < 1 || n_kv_heads < 1)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "cache dimensions must be positive");
+  if (head_dim != 64 && head_dim != 128)
+    return fail(ctx, GLA_ERR_NOT_SUPPORTED, "Q8 cache: head_dim 64 or 128");
+  const size_t rows = (size_t)n_layers * context_length;
+  const size_t vbytes = rows * n_kv_heads * head_dim;
+  const size_t sbytes = rows * n_kv_heads * 8 * sizeof(uint16_t);
+  DeviceGuard dg(ctx->device);
+  void *k = nullptr, *v = nullptr, *sc = nullptr;
+  if (cudaMalloc(&k, vbytes) != cudaSuccess || cudaMalloc(&v, vbytes) != cudaSuccess ||
+      cudaMalloc(&sc, sbytes) != cudaSuccess) {
+    cudaFree(k);
+    cudaFree(v);
+    cudaGetLastError();
+    return fail(ctx, GLA_ERR_OUT_OF_MEMORY, "Q8 KV cache allocation failed");
+  }
+  cudaMemsetAsync(k, 0, vbytes, ctx->stream);
+  cudaMemsetAsync(v, 0, vbytes, ctx->stream);
+  cudaMemsetAsync(sc, 0, sbytes, ctx->stream);
+  *key_cache = static_cast<int8_t*>(k);
+  *value_cache = static_cast<int8_t*>(v);
+  *scales = static_cast<uint16_t*>(sc);
+  return GLA_OK;
+}
+
+int32_t gla_kv_cache_free_q8(gla_ctx* ctx, int8_t* key_cache, int8_t* value_cache,
+                             uint16_t* scales) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  DeviceGuard dg(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  cudaFree(key_cache);
+  cudaFree(value_cache);
+  cudaFree(scales);
+  return GLA_OK;
+}
+
+int32_t gla_rope_append_q8(gla_ctx* ctx, float* q, float* k, const float* v, int8_t* key_cache,
+                           int8_t* value_cache, uint16_t* scales, int32_t n_heads,
+                           int32_t n_kv_heads, int32_t head_dim, const int32_t* position_holder,
+                           int32_t context_length, float theta, int32_t rope_style) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  if (!q || !k || !v || !key_cache || !value_cache || !scales || !position_holder)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "null pointer");
+  if (n_heads < 1 || n_kv_heads < 1 || n_kv_heads > n_heads || context_length < 1)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "bad RoPE shape");
+  if (head_dim != 64 && head_dim != 128)
+    return fail(ctx, GLA_ERR_NOT_SUPPORTED, "Q8 cache: head_dim 64 or 128");
+  if (rope_style != GLA_ROPE_INTERLEAVED && rope_style != GLA_ROPE_NEOX)
+    return fail(ctx, GLA_ERR_INVALID_ARG, "unknown rope_style");
+  if (!(theta > 0.f)) return fail(ctx, GLA_ERR_INVALID_ARG, "theta must be positive");
+  DeviceGuard dg(ctx->device);
+  std::string err;
+  int rc = gla::launch_rope_append_q8(q, k, v, key_cache, value_cache, scales, n_heads, n_kv_heads,
+                                      head_dim, position_holder, context_length, theta,
+                                      rope_style, ctx->status, ctx->stream, &err);
+  return rc == GLA_OK ? GLA_OK : fail(ctx, rc, err);
+}
+
 int32_t gla_decode_batched_f32kv(gla_ctx* ctx, const float* q, const float* const* k_ptrs,
                                  const float* const* v_ptrs, const int32_t* n_pos,
                                  int32_t max_n_pos, float* xb, int32_t batch, int32_t n_heads,

@@ -94,6 +94,13 @@ int launch_quantize_q8(const float* k, const float* v, int64_t src_stride, int32
                        int32_t n_kv, int32_t hd, int8_t* kq, int8_t* vq, int64_t kv_stride,
                        uint16_t* scales, cudaStream_t stream, std::string* err);
 
+// RoPE of the new token + its k/v quantised into a Q8 cache row (q8.cu).
+int launch_rope_append_q8(float* q, float* k, const float* v, int8_t* kq, int8_t* vq,
+                          uint16_t* scales, int32_t n_heads, int32_t n_kv, int32_t hd,
+                          const int32_t* position_holder, int32_t context_length, float theta,
+                          int32_t rope_style, int32_t* status, cudaStream_t stream,
+                          std::string* err);
+
 // Output projection + residual (wo.cu): x[i] += w[i][:] . xb, w FP16 [d][n].
 int launch_wo_residual_f16(const uint16_t* w, const float* xb, float* x, int32_t n, int32_t d,
                            const DeviceInfo& dev, cudaStream_t stream, std::string* err);

@@ -16,6 +16,7 @@
 
 #include "decode_kernel.cuh"
 #include "gla_internal.h"
+#include "gla_rope.cuh"
 
 namespace gla {
 
@@ -65,7 +66,88 @@ __global__ void quantize_q8_kernel(const float* __restrict__ k, const float* __r
   }
 }
 
+// The new token: RoPE of q and k in place (the same helpers and rounding as
+// the FP32 RoPE kernel), then k and v quantised into row `position` of a Q8
+// cache.  One warp per head: warps [0, n_kv) rotate kv head g's k (through
+// shared memory) and quantise k and v, warps [n_kv, n_kv + n_heads) rotate q.
+// A position outside [0, context_length) writes nothing and latches
+// GLA_ERR_INVALID_ARG in the status word.
+__global__ void __launch_bounds__(128)
+    rope_append_q8_kernel(float* __restrict__ q, float* __restrict__ k,
+                          const float* __restrict__ v, int8_t* __restrict__ kq,
+                          int8_t* __restrict__ vq, uint16_t* __restrict__ scales, int32_t n_heads,
+                          int32_t n_kv, int32_t hd, const int32_t* __restrict__ position_holder,
+                          int32_t context_length, double theta, int32_t style,
+                          int32_t* __restrict__ status) {
+  __shared__ float s_row[4][128];
+  // programmatic dependent launch, as the FP32 RoPE kernel: memory only after
+  // the preceding kernel, dependents released at once
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int w = blockIdx.x * 4 + warp;
+  if (w >= n_kv + n_heads) return;
+  const int pos = position_holder[0];
+  if (pos < 0 || pos >= context_length) {
+    if (lane == 0) atomicCAS(status, 0, GLA_ERR_INVALID_ARG);
+    return;
+  }
+  const bool is_k = w < n_kv;
+  const int h = is_k ? w : w - n_kv;
+  float* x = (is_k ? k : q) + (int64_t)h * hd;
+  for (int ic = lane; ic < hd / 2; ic += 32) {
+    float fcr, fci;
+    rope_cos_sin(pos, ic, hd, theta, &fcr, &fci);
+    int i0, i1;
+    rope_pair(style, ic, hd, &i0, &i1);
+    float o0, o1;
+    rope_rotate(x[i0], x[i1], fcr, fci, &o0, &o1);
+    x[i0] = o0;
+    x[i1] = o1;
+    if (is_k) {
+      s_row[warp][i0] = o0;
+      s_row[warp][i1] = o1;
+    }
+  }
+  if (!is_k) return;
+  __syncwarp();
+  const int64_t row = (int64_t)pos * n_kv * hd + (int64_t)h * hd;
+  const int nb = hd / 32;
+  const uint16_t ks = quantize_head_row(s_row[warp], kq + row, nb, lane);
+  const uint16_t vs = quantize_head_row(v + (int64_t)h * hd, vq + row, nb, lane);
+  uint16_t* srow = scales + ((int64_t)pos * n_kv + h) * kQ8ScaleHalves;
+  if (lane < 4) {
+    srow[lane] = lane < nb ? ks : (uint16_t)0;
+    srow[4 + lane] = lane < nb ? vs : (uint16_t)0;
+  }
+}
+
 }  // namespace
+
+int launch_rope_append_q8(float* q, float* k, const float* v, int8_t* kq, int8_t* vq,
+                          uint16_t* scales, int32_t n_heads, int32_t n_kv, int32_t hd,
+                          const int32_t* position_holder, int32_t context_length, float theta,
+                          int32_t rope_style, int32_t* status, cudaStream_t stream,
+                          std::string* err) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((n_kv + n_heads + 3) / 4);
+  cfg.blockDim = dim3(128);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, rope_append_q8_kernel, q, k, v, kq, vq, scales, n_heads,
+                                     n_kv, hd, position_holder, context_length, (double)theta,
+                                     rope_style, status);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    *err = std::string("rope/Q8 append launch failed: ") + cudaGetErrorString(e);
+    return GLA_ERR_CUDA;
+  }
+  return GLA_OK;
+}
 
 int launch_quantize_q8(const float* k, const float* v, int64_t src_stride, int32_t n_rows,
                        int32_t n_kv, int32_t hd, int8_t* kq, int8_t* vq, int64_t kv_stride,

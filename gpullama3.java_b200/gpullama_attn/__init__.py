@@ -22,6 +22,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libgpullama
 GLA_OK = 0
 DTYPE_F32 = 0
 DTYPE_F16 = 1
+DTYPE_Q8 = 2
 ROPE_INTERLEAVED = 0
 ROPE_NEOX = 1
 OPT_EARLY_KV_PREFETCH = 1  # values: 0 off, 1 host n_pos, 2 (default) also device positions
@@ -82,6 +83,10 @@ _SIGS = {
     "gla_wo_residual_f16": (_I32, [_P, _P, _P, _P, _I32, _I32]),
     "gla_decode_q8kv": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F]),
     "gla_kv_quantize_q8": (_I32, [_P, _P, _P, _I64, _I32, _I32, _I32, _P, _P, _I64, _P]),
+    "gla_kv_cache_alloc_q8": (_I32, [_P, _I32, _I32, _I32, _I32, _P, _P, _P]),
+    "gla_kv_cache_free_q8": (_I32, [_P, _P, _P, _P]),
+    "gla_rope_append_q8": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P, _I32, _F,
+                                  _I32]),
     "gla_ingest_prompt_f32": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
                                      _I32, _F, _I32]),
     "gla_ingest_prompt_f16kv": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
@@ -333,6 +338,26 @@ class Context:
         self._check(self._L.gla_kv_quantize_q8(self._h, _ptr(k), _ptr(v), src_stride, n_rows,
                                                n_kv_heads, head_dim, _ptr(kq), _ptr(vq),
                                                kv_stride, _ptr(scales)), "gla_kv_quantize_q8")
+
+    def rope_append_q8(self, q, k, v, kq, vq, scales, n_heads, n_kv_heads, head_dim,
+                       position_holder, context_length, theta, style=ROPE_INTERLEAVED):
+        """gla_rope_append_q8: RoPE of the new token, k/v quantised into a Q8 cache row."""
+        self._check(self._L.gla_rope_append_q8(self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(kq),
+                                               _ptr(vq), _ptr(scales), n_heads, n_kv_heads,
+                                               head_dim, _ptr(position_holder), context_length,
+                                               theta, style), "gla_rope_append_q8")
+
+    def kv_cache_alloc_q8(self, n_layers, context_length, n_kv_heads, head_dim):
+        """gla_kv_cache_alloc_q8: returns (k, v, scales) device addresses."""
+        k, v, s = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        self._check(self._L.gla_kv_cache_alloc_q8(self._h, n_layers, context_length, n_kv_heads,
+                                                  head_dim, ctypes.byref(k), ctypes.byref(v),
+                                                  ctypes.byref(s)), "gla_kv_cache_alloc_q8")
+        return k.value, v.value, s.value
+
+    def kv_cache_free_q8(self, k, v, scales):
+        self._check(self._L.gla_kv_cache_free_q8(self._h, ctypes.c_void_p(k), ctypes.c_void_p(v),
+                                                 ctypes.c_void_p(scales)), "gla_kv_cache_free_q8")
 
     def wo_residual(self, xb, x, w, n, d):
         """gla_wo_residual_f16: x += w . xb (w FP16 [d][n])."""

@@ -226,6 +226,29 @@ int32_t gla_kv_quantize_q8(gla_ctx* ctx, const float* k, const float* v, int64_t
                            int32_t n_rows, int32_t n_kv_heads, int32_t head_dim, int8_t* kq,
                            int8_t* vq, int64_t kv_stride, uint16_t* scales);
 
+/* Zero-initialised Q8 caches for n_layers layers (the Q8 counterpart of
+ * gla_kv_cache_alloc, i.e. of the State allocation, state/LlamaState.java:45-46):
+ * k, v int8 [layer][context_length][n_kv_heads*head_dim], scales FP16
+ * [layer][context_length][n_kv_heads][8]; layer l starts at
+ * l*context_length*n_kv_heads*head_dim (values) and l*context_length*n_kv_heads*8
+ * (scales).  head_dim 64 or 128. */
+int32_t gla_kv_cache_alloc_q8(gla_ctx* ctx, int32_t n_layers, int32_t context_length,
+                              int32_t n_kv_heads, int32_t head_dim, int8_t** key_cache,
+                              int8_t** value_cache, uint16_t** scales);
+int32_t gla_kv_cache_free_q8(gla_ctx* ctx, int8_t* key_cache, int8_t* value_cache,
+                             uint16_t* scales);
+
+/* The new token into a Q8 cache layer: RoPE of q and k in place as
+ * gla_rope_append_f32 does (same bits), then k and v quantised (as
+ * gla_kv_quantize_q8) into row position_holder[0] of the layer's
+ * key_cache/value_cache [context_length][kv_dim] and scales
+ * [context_length][n_kv_heads][8].  A position outside [0, context_length)
+ * writes nothing and latches GLA_ERR_INVALID_ARG in the device status. */
+int32_t gla_rope_append_q8(gla_ctx* ctx, float* q, float* k, const float* v, int8_t* key_cache,
+                           int8_t* value_cache, uint16_t* scales, int32_t n_heads,
+                           int32_t n_kv_heads, int32_t head_dim, const int32_t* position_holder,
+                           int32_t context_length, float theta, int32_t rope_style);
+
 /* Batched decode: `batch` independent sequences, one new token each.
  *  q  [batch][n_heads][head_dim], xb [batch][n_heads][head_dim]
  *  k_ptrs/v_ptrs: DEVICE arrays of `batch` layer-base pointers

@@ -124,3 +124,75 @@ def test_decode_q8_rejects_bad_arguments(gla_ctx):
         gla_ctx.decode_q8(xb, kq, kq, sc, xb, 8, 8, 128, 10, kv_stride=8 * 128 + 8)
     with pytest.raises(gla.GlaError):  # scales not 16-byte aligned
         gla_ctx.decode_q8(xb, kq, kq, sc.view(-1)[1:], xb, 8, 8, 128, 10)
+
+
+def test_q8_token_flow_alloc_rope_append_decode(gla_ctx, oracle):
+    """The per-token flow over a Q8 cache layer from gla_kv_cache_alloc_q8:
+    history rows quantised, the new token's q/k rotated and k/v appended by
+    gla_rope_append_q8 at the device position, then gla_decode_q8kv.  The
+    appended row equals the oracle quantiser applied to the rotated k (bit for
+    bit); q and k are rotated like the FP32 RoPE (atol 2e-6); attention matches
+    the FP32 oracle on the dequantised cache; untouched rows stay zero."""
+    import gpullama_attn as gla
+
+    torch = _torch()
+    nh, nkv, hd, T, ctx_len, layers, theta = 24, 8, 128, 700, 1024, 2, 500000.0
+    kvd = nkv * hd
+    kp, vp, sp = gla_ctx.kv_cache_alloc_q8(layers, ctx_len, nkv, hd)
+    try:
+        layer = 1
+        kl = kp + layer * ctx_len * kvd
+        vl = vp + layer * ctx_len * kvd
+        sl = sp + layer * ctx_len * nkv * 8 * 2  # bytes
+        rng = np.random.Generator(np.random.PCG64(77))
+        hist_k = rng.standard_normal((T - 1, kvd), dtype=np.float32)
+        hist_v = rng.standard_normal((T - 1, kvd), dtype=np.float32)
+        gla_ctx.quantize_q8(_dev(hist_k), _dev(hist_v), T - 1, nkv, hd, kl, vl, sl)
+        q = rng.standard_normal(nh * hd, dtype=np.float32)
+        kn = rng.standard_normal(kvd, dtype=np.float32)
+        vn = rng.standard_normal(kvd, dtype=np.float32)
+        qd, kd, vd = _dev(q), _dev(kn), _dev(vn)
+        ph = torch.tensor([T - 1], dtype=torch.int32, device="cuda")
+        gla_ctx.rope_append_q8(qd, kd, vd, kl, vl, sl, nh, nkv, hd, ph, ctx_len, theta,
+                               gla.ROPE_INTERLEAVED)
+        xb = torch.empty(nh * hd, device="cuda")
+        gla_ctx.decode_q8(qd, kl, vl, sl, xb, nh, nkv, hd, T)
+        assert gla_ctx.device_status() == 0
+
+        # the layer read back through views of the raw device addresses
+        def view(ptr, shape, typestr):
+            class _Mem:
+                __cuda_array_interface__ = {"shape": shape, "typestr": typestr,
+                                            "data": (ptr, False), "version": 3, "strides": None}
+            return torch.as_tensor(_Mem(), device="cuda").cpu().numpy()
+
+        ck = view(kl, (ctx_len, kvd), "|i1")
+        cv = view(vl, (ctx_len, kvd), "|i1")
+        cs = view(sl, (ctx_len, nkv, 8), "<u2")
+        assert (ck[T:] == 0).all() and (cv[T:] == 0).all() and (cs[T:] == 0).all()
+        q_rot, k_rot = qd.cpu().numpy(), kd.cpu().numpy()
+        cr, ci = oracle.rope_freqs(ctx_len, hd, theta)
+        qr, kr = q.copy(), kn.copy()
+        oracle.rope_interleaved(qr, kr, hd, T - 1, cr, ci)
+        np.testing.assert_allclose(q_rot, qr, rtol=0, atol=2e-6)
+        np.testing.assert_allclose(k_rot, kr, rtol=0, atol=2e-6)
+        rq, rv, rs = oracle.quantize_q8(k_rot[None], vn[None], nkv, hd)
+        np.testing.assert_array_equal(ck[T - 1], rq[0])
+        np.testing.assert_array_equal(cv[T - 1], rv[0])
+        np.testing.assert_array_equal(cs[T - 1], rs[0])
+        hq, hv, hs = oracle.quantize_q8(hist_k, hist_v, nkv, hd)
+        np.testing.assert_array_equal(ck[:T - 1], hq)
+        np.testing.assert_array_equal(cs[:T - 1], hs)
+        kd_all, vd_all = oracle.dequantize_q8(ck[:T], cv[:T], cs[:T], nkv, hd)
+        ref = oracle.decode_f32(q_rot, kd_all, vd_all, nh, nkv, hd, T)
+        got = xb.cpu().numpy()
+        err = np.abs(got - ref).max()
+        assert err <= TOL and err / np.abs(ref).max() <= TOL, err
+        # a position past the context writes nothing and latches an error
+        ph_bad = torch.tensor([ctx_len], dtype=torch.int32, device="cuda")
+        gla_ctx.rope_append_q8(qd, kd, vd, kl, vl, sl, nh, nkv, hd, ph_bad, ctx_len, theta,
+                               gla.ROPE_INTERLEAVED)
+        assert gla_ctx.device_status() == -1  # GLA_ERR_INVALID_ARG, then cleared
+        assert gla_ctx.device_status() == 0
+    finally:
+        gla_ctx.kv_cache_free_q8(kp, vp, sp)
