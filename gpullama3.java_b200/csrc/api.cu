@@ -225,6 +225,9 @@ int process_heads(gla_ctx* ctx, int dtype, const float* q, const void* key_cache
   if (rc != GLA_OK) return rc;
   if (!aligned16(q) || !aligned16(key_cache) || !aligned16(value_cache) || !aligned16(xb))
     return fail(ctx, GLA_ERR_ALIGNMENT, "q, caches and xb must be 16-byte aligned");
+  if (rope && (!rope->k || !rope->v)) return fail(ctx, GLA_ERR_INVALID_ARG, "null pointer");
+  if (rope && (!aligned16(rope->k) || !aligned16(rope->v)))
+    return fail(ctx, GLA_ERR_ALIGNMENT, "k and v must be 16-byte aligned");
   DeviceGuard dg(ctx->device);
   if (!dg.ok) return fail(ctx, GLA_ERR_CUDA, "cudaSetDevice failed");
   const int64_t loff = (int64_t)layer * context_length * kv_dim * esize;  // 64-bit layer offset

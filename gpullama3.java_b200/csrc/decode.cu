@@ -53,7 +53,7 @@ Layout layout_for(int dtype, int hd, int group, int tile, int stages, int batch,
   Layout L;
   size_t off = (size_t)stages * stage_bytes_for(dtype, hd, tile);
   L.off_bars = (int32_t)align16(off);
-  off = L.off_bars + (size_t)stages * 2 * sizeof(uint64_t);
+  off = L.off_bars + (size_t)(stages * 2 + 1) * sizeof(uint64_t);  // full, empty, late
   L.off_seq = (int32_t)align16(off);
   off = L.off_seq + (size_t)(3 * batch + 1) * sizeof(int32_t);
   L.off_q = (int32_t)align16(off);

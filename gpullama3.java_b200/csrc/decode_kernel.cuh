@@ -869,6 +869,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bars);
   uint64_t* empty = full + a.stages;
+  uint64_t* late_bar = empty + a.stages;  // fused RoPE: the newest-row tile's early copy
   int32_t* seq_start = reinterpret_cast<int32_t*>(smem + a.off_seq);  // [B+1] (units)
   int32_t* nunits = seq_start + (B + 1);                              // [B]
   int32_t* npos = nunits + B;                                         // [B]
@@ -883,6 +884,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
       mbar_init(&full[s], LOADER == 0 ? 1 : 32);
       mbar_init(&empty[s], NW);
     }
+    mbar_init(late_bar, 1);
     flags[0] = 0;
     flags[1] = 0;
     flags[2] = 0;
@@ -937,6 +939,41 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
   // and value row are written at row n_pos - 1 of the caches, then a proxy
   // fence orders those generic stores before the tensor copy that reads the
   // row back (only the CTA holding that row's tile does this).
+  // Fused RoPE, early-prefetched newest-row tile (stage st, row r of the
+  // tile): the producer warp writes kv head g's rotated key row and value row
+  // to the caches (for later calls) and over the stale row of the staged tile
+  // (128B-swizzled FP32 layout), after the stage's early copy has landed.
+  auto append_row_stage = [&](int g, int st, int r) {
+    if constexpr (Consumer::kElemBytes != 4) return;  // fused RoPE writes FP32 caches only
+    const int pos = npos[0] - 1;
+    float* kc = const_cast<float*>(static_cast<const float*>(a.k)) + (int64_t)pos * a.kv_stride +
+                (int64_t)g * HD;
+    float* vc = const_cast<float*>(static_cast<const float*>(a.v)) + (int64_t)pos * a.kv_stride +
+                (int64_t)g * HD;
+    const float* kn = a.rope_k + (int64_t)g * HD;
+    const float* vn = a.rope_v + (int64_t)g * HD;
+    char* ks = smem + (size_t)st * a.stage_bytes;
+    char* vs = ks + (size_t)a.tile * HD * esize;
+    auto at = [&](char* base, int col) {
+      return reinterpret_cast<float*>(base + TL::chunk_off(a.tile, r, col & ~3) + (col & 3) * 4);
+    };
+    for (int ic = lane; ic < HD / 2; ic += 32) {
+      int i0, i1;
+      rope_pair(a.rope_style, ic, HD, &i0, &i1);
+      const float2 cs = rope_cs[ic];
+      float o0, o1;
+      rope_rotate(kn[i0], kn[i1], cs.x, cs.y, &o0, &o1);
+      const float v0 = vn[i0], v1 = vn[i1];
+      kc[i0] = o0;
+      kc[i1] = o1;
+      vc[i0] = v0;
+      vc[i1] = v1;
+      *at(ks, i0) = o0;
+      *at(ks, i1) = o1;
+      *at(vs, i0) = v0;
+      *at(vs, i1) = v1;
+    }
+  };
   auto append_row = [&](int g) {
     if constexpr (Consumer::kElemBytes != 4) return;  // fused RoPE writes FP32 caches only
     const int pos = npos[0] - 1;
@@ -963,22 +1000,23 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
   // TMA loads of one tile (LOADER 0): whole boxes of `tile` rows; rows past
   // the tensor map's extent are zero-filled, so the byte count is the boxes'
   // size.  Rows past n_pos inside the extent are loaded and masked later.
-  auto tma_tile = [&](int st, const Tile& t, uint64_t pol) {
+  auto tma_tile = [&](int st, const Tile& t, uint64_t pol, uint64_t* bar = nullptr) {
     char* ks = smem + (size_t)st * a.stage_bytes;
     char* vs = ks + (size_t)a.tile * HD * esize;
-    mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * a.tile * HD * esize +
-                                                (Consumer::kQ8 ? a.tile * kQ8ScaleRowBytes : 0)));
+    if (bar == nullptr) bar = &full[st];
+    mbar_arrive_expect_tx(bar, (uint32_t)(2 * a.tile * HD * esize +
+                                          (Consumer::kQ8 ? a.tile * kQ8ScaleRowBytes : 0)));
 #pragma unroll
     for (int cb = 0; cb < TL::kBlocks; ++cb) {
       const int x = t.g * HD + cb * TL::kCW;
       const size_t off = (size_t)cb * a.tile * TL::kRowB;
-      tma_load_2d(ks + off, &a.tmap_k, x, t.row0, &full[st], pol);
-      tma_load_2d(vs + off, &a.tmap_v, x, t.row0, &full[st], pol);
+      tma_load_2d(ks + off, &a.tmap_k, x, t.row0, bar, pol);
+      tma_load_2d(vs + off, &a.tmap_v, x, t.row0, bar, pol);
     }
     // Q8 cache: the K and V block scales of kv head g, one 16-byte row a key
     if constexpr (Consumer::kQ8)
       tma_load_2d(ks + (size_t)2 * a.tile * HD, &a.tmap_s, t.g * kQ8ScaleHalves, t.row0,
-                  &full[st], pol);
+                  bar, pol);
   };
   // Early KV prefetch (programmatic dependent launch).  The work partition
   // needs only the positions, so the producer may start streaming this CTA's
@@ -1009,9 +1047,25 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
       TileWalk wk;
       wk.init(seq_start, nunits, B, lo, lo + cnt);
       Tile t;
+      int32_t seg = -1;
       while (n_early < a.stages && wk.next(nunits, B, n_kv, tile_units, unit_rows, t)) {
-        if (t.row0 + t.units * unit_rows >= npos[t.b]) late |= 1u << n_early;  // newest row
-        else tma_tile(n_early, t, pol);
+        // fused RoPE: warm L2 with the inputs read right after the wait (the
+        // group's q vectors, the new key and value rows of kv head g)
+        if (a.rope && t.b * n_kv + t.g != seg) {
+          seg = t.b * n_kv + t.g;
+          prefetch_l2_bulk(a.q + ((int64_t)t.b * a.n_heads + (int64_t)t.g * G) * HD,
+                           (uint32_t)(G * HD * sizeof(float)));
+          prefetch_l2_bulk(a.rope_k + (int64_t)t.g * HD, (uint32_t)(HD * sizeof(float)));
+          prefetch_l2_bulk(a.rope_v + (int64_t)t.g * HD, (uint32_t)(HD * sizeof(float)));
+        }
+        if (t.row0 + t.units * unit_rows >= npos[t.b]) {  // newest row
+          late |= 1u << n_early;
+          // fused RoPE: fetch the tile now (its newest row is stale) and
+          // overwrite that row in shared memory after the wait
+          if (a.rope) tma_tile(n_early, t, pol, late_bar);
+        } else {
+          tma_tile(n_early, t, pol);
+        }
         ++n_early;
       }
     }
@@ -1044,8 +1098,16 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
       for (int32_t k = 0; k < first; ++k) {  // first ring pass: no empty-barrier waits
         wk.next(nunits, B, n_kv, tile_units, unit_rows, t);
         if ((late_mask >> k) & 1u) {
-          if (a.rope) append_row(t.g);
-          if (lane == 0) tma_tile(k, t, pol);
+          if (a.rope) {
+            bool landed = true;
+            if (lane == 0) landed = mbar_wait(late_bar, 0, flags, a.status);
+            landed = __shfl_sync(0xffffffffu, landed, 0);
+            if (landed) append_row_stage(t.g, k, npos[0] - 1 - t.row0);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[k]);  // the stage's only arrival this pass
+          } else if (lane == 0) {
+            tma_tile(k, t, pol);
+          }
         }
       }
       __syncwarp();

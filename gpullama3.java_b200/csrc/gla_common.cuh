@@ -293,6 +293,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// L2 prefetch of `bytes` (a multiple of 16) from a 16-byte aligned address: a
+// hint only (L2 is the coherence point), safe while another kernel writes it.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Tiled TMA load of a 2D box at (x, y) of `tmap` (a __grid_constant__ kernel
 // parameter) into shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tmap, int32_t x,

@@ -167,7 +167,8 @@ int32_t gla_process_heads_flash_attention(gla_ctx* ctx, const float* q, const fl
  * as those two calls in a row.  q and k are read, not rotated in place.
  * Replaces the rope, copyToCache and parallel-attention tasks of one layer
  * (TransformerComputeKernelsLayered.java:129-139, :179-205, :336-458); no
- * single reference counterpart.  k, v: [kvDim] rows of the new token. */
+ * single reference counterpart.  k, v: [kvDim] rows of the new token; q, k,
+ * v, the caches and xb 16-byte aligned. */
 int32_t gla_rope_append_attention_f32(gla_ctx* ctx, const float* q, const float* k,
                                       const float* v, float* key_cache, float* value_cache,
                                       float* xb, int32_t n_heads, int32_t head_size,
