@@ -37,7 +37,9 @@ __device__ __forceinline__ uint16_t quantize_head_row(const float* __restrict__ 
     const float v = x[32 * b + lane];
     const float amax = warp_max(fabsf(v));
     const float d = amax / 127.0f;
-    const float id = d != 0.0f ? 1.0f / d : 0.0f;
+    // d below ~1e-38 makes 1/d overflow; such a block's FP16 scale is 0 anyway
+    const float r = 1.0f / d;
+    const float id = (d != 0.0f && r < INFINITY) ? r : 0.0f;
     out[32 * b + lane] = (int8_t)roundf(__fmul_rn(v, id));
     if (lane == b) mine = __half_as_ushort(__float2half_rn(d));
   }

@@ -377,7 +377,9 @@ static void quantize_head_row(const float* x, int8_t* q, uint16_t* s, int nb) {
       if (ax > amax) amax = ax;
     }
     const float d = amax / 127.0f;
-    const float id = d != 0.0f ? 1.0f / d : 0.0f;
+    /* d below ~1e-38 makes 1/d overflow; such a block's FP16 scale is 0 anyway */
+    const float r = d != 0.0f ? 1.0f / d : 0.0f;
+    const float id = (d != 0.0f && r < INFINITY) ? r : 0.0f;
     for (int j = 0; j < 32; ++j) q[32 * b + j] = (int8_t)roundf(x[32 * b + j] * id);
     s[b] = float_to_half_rne(d);
   }

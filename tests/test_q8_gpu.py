@@ -48,6 +48,7 @@ def test_quantize_matches_oracle_bitwise(gla_ctx, oracle, rows, n_kv, hd, pad):
     k[1, 32:64] = 1e-30       # tiny values
     v[2, :hd] *= 1e4          # large values
     k[3, 5] = -127.5          # exact ties
+    v[4, 32:64] = 1e-39       # subnormal block: 1/d overflows, q = 0
     kq, vq, sc = _quantize_gpu(gla_ctx, k, v, n_kv, hd, n_kv * hd + pad)
     rq, rv, rs = oracle.quantize_q8(k, v, n_kv, hd)
     np.testing.assert_array_equal(kq[:, :n_kv * hd], rq)
