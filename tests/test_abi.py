@@ -44,6 +44,17 @@ def test_null_context_is_rejected():
                                                0, 16) == -1
     assert L.gla_lse_combine(None, None, 1, 1, 1, None) == -1
     assert L.gla_prefill_causal_f16(None, None, None, None, None, 8, 4, 4, 64, 0.1) == -1
+    assert L.gla_ingest_prompt_f32(None, None, None, None, None, None, None, 0, 4, 8, 2, 64, 16,
+                                   1e4, 0) == -1
+    assert L.gla_ingest_prompt_f16kv(None, None, None, None, None, None, None, 0, 4, 8, 2, 64,
+                                     16, 1e4, 0) == -1
+    assert L.gla_wo_residual_f16(None, None, None, None, 64, 64) == -1
+    assert L.gla_decode_q8kv(None, None, None, None, None, None, 8, 2, 64, 128, 1, 0.125) == -1
+    assert L.gla_kv_quantize_q8(None, None, None, 128, 1, 2, 64, None, None, 128, None) == -1
+    assert L.gla_kv_cache_alloc_q8(None, 1, 16, 2, 64, None, None, None) == -1
+    assert L.gla_kv_cache_free_q8(None, None, None, None) == -1
+    assert L.gla_rope_append_q8(None, None, None, None, None, None, None, 8, 2, 64, None, 16, 1e4,
+                                0) == -1
     assert L.gla_destroy(None) == -1
     assert L.gla_device_status(None, None) == -1
     assert L.gla_last_error(None) == b""
