@@ -361,20 +361,28 @@ def test_fused_rope_append_attention_equals_separate_calls(gla_ctx, style, hd, n
     gla_ctx.rope_append(q1, k1, v1, kc1[layer], vc1[layer], nh, nkv, hd, ph, theta, style)
     gla_ctx.process_heads_flash_attention(q1, kc1, vc1, xb1, nh, hd, kvd, nh // nkv, ph, layer,
                                           ctxlen)
-    kc2, vc2, q2, k2, v2 = dev(kc0), dev(vc0), dev(q0), dev(k0), dev(v0)
-    xb2 = torch.empty(nh * hd, device="cuda")
-    scratch = torch.empty(nh * hd, device="cuda")
-    for _ in range(3):  # decodes that release their dependents early
-        gla_ctx.decode(q2, kc2[0], vc2[0], scratch, nh, nkv, hd, ctxlen)
-    gla_ctx.rope_append_attention(q2, k2, v2, kc2, vc2, xb2, nh, hd, kvd, nh // nkv, ph, layer,
-                                  ctxlen, theta, style)
-    assert gla_ctx.device_status() == 0
-    np.testing.assert_array_equal(xb2.cpu().numpy(), xb1.cpu().numpy())
-    np.testing.assert_array_equal(kc2.cpu().numpy(), kc1.cpu().numpy())
-    np.testing.assert_array_equal(vc2.cpu().numpy(), vc1.cpu().numpy())
-    np.testing.assert_array_equal(q2.cpu().numpy(), q0)
-    changed = np.argwhere(np.any(kc2.cpu().numpy() != kc0, axis=-1))
-    assert changed.tolist() == [[layer, pos]]
+    # every early-prefetch level: 2 patches the newest row into the tile
+    # copied early, 0 and 1 (position on the device) append it to the cache
+    # and copy the tile after the wait
+    try:
+        for opt in (2, 1, 0):
+            gla_ctx.set_option(gla.OPT_EARLY_KV_PREFETCH, opt)
+            kc2, vc2, q2, k2, v2 = dev(kc0), dev(vc0), dev(q0), dev(k0), dev(v0)
+            xb2 = torch.empty(nh * hd, device="cuda")
+            scratch = torch.empty(nh * hd, device="cuda")
+            for _ in range(3):  # decodes that release their dependents early
+                gla_ctx.decode(q2, kc2[0], vc2[0], scratch, nh, nkv, hd, ctxlen)
+            gla_ctx.rope_append_attention(q2, k2, v2, kc2, vc2, xb2, nh, hd, kvd, nh // nkv, ph,
+                                          layer, ctxlen, theta, style)
+            assert gla_ctx.device_status() == 0
+            np.testing.assert_array_equal(xb2.cpu().numpy(), xb1.cpu().numpy())
+            np.testing.assert_array_equal(kc2.cpu().numpy(), kc1.cpu().numpy())
+            np.testing.assert_array_equal(vc2.cpu().numpy(), vc1.cpu().numpy())
+            np.testing.assert_array_equal(q2.cpu().numpy(), q0)
+            changed = np.argwhere(np.any(kc2.cpu().numpy() != kc0, axis=-1))
+            assert changed.tolist() == [[layer, pos]]
+    finally:
+        gla_ctx.set_option(gla.OPT_EARLY_KV_PREFETCH, 2)
     with pytest.raises(gla.GlaError):
         gla_ctx.rope_append_attention(q2, k2, v2, kc2, vc2, xb2, nh, hd, kvd, nh // nkv, ph,
                                       layer, ctxlen, theta, 7)
