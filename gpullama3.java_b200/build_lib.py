@@ -20,7 +20,7 @@ OUT = os.path.join(HERE, "gpullama_attn", "libgpullama_attn.so")
 INCLUDE = os.path.normpath(os.path.join(HERE, "..", "include"))
 
 SOURCES = ["api.cu", "decode.cu", "combine.cu", "rope.cu", "prefill.cu", "comm.cpp", "peer.cpp",
-           "noalloc.cu", "ingest.cu", "wo.cu", "q8.cu"]
+           "noalloc.cu", "ingest.cu", "wo.cu", "q8.cu", "debug.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
               "-I", INCLUDE]

@@ -26,8 +26,10 @@ struct gla_ctx {
   int32_t* status = nullptr;        // device status word
   int32_t* counters = nullptr;      // piece counters (zero between calls)
   size_t counters_cap = 0;
-  float* parts = nullptr;           // piece slots
-  size_t parts_cap = 0;             // floats
+  uint64_t* parts = nullptr;        // piece slots (tagged 64-bit words, zeroed at allocation)
+  size_t parts_cap = 0;             // words
+  uint64_t* trace = nullptr;        // GLA_OPT_TRACE: per-CTA phase stamps of the last decode
+  size_t trace_words = 0;
   float* records = nullptr;         // sharded decode: local records
   float* gathered = nullptr;        // sharded decode: all ranks' records
   size_t records_cap = 0;           // floats per rank
@@ -53,6 +55,10 @@ int cuda_fail(gla_ctx* ctx, cudaError_t e, const char* what) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// The context's 256-byte status block: the device status word at 0, the
+// decode call-epoch word (see DecodeWorkspace) at kEpochOffset.
+constexpr size_t kEpochOffset = 64;
+
 // Makes the context's device current for the duration of a call.
 struct DeviceGuard {
   int prev = -1;
@@ -73,20 +79,23 @@ bool stream_capturing(cudaStream_t s) {
 }
 
 // Grows the piece workspace; never during stream capture.
-int ensure_workspace(gla_ctx* ctx, size_t part_floats, size_t counters) {
-  if (part_floats <= ctx->parts_cap && counters <= ctx->counters_cap) return GLA_OK;
+int ensure_workspace(gla_ctx* ctx, size_t part_words, size_t counters) {
+  if (part_words <= ctx->parts_cap && counters <= ctx->counters_cap) return GLA_OK;
   if (stream_capturing(ctx->stream))
     return fail(ctx, GLA_ERR_INVALID_ARG,
                 "decode workspace must grow; call gla_reserve before stream capture");
   cudaError_t e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamSynchronize");
-  if (part_floats > ctx->parts_cap) {
-    size_t cap = std::max(part_floats, ctx->parts_cap * 2);
+  if (part_words > ctx->parts_cap) {
+    size_t cap = std::max(part_words, ctx->parts_cap * 2);
     cudaFree(ctx->parts);
     ctx->parts = nullptr;
     ctx->parts_cap = 0;
-    e = cudaMalloc(&ctx->parts, cap * sizeof(float));
+    e = cudaMalloc(&ctx->parts, cap * sizeof(uint64_t));
     if (e != cudaSuccess) return fail(ctx, GLA_ERR_OUT_OF_MEMORY, "workspace allocation failed");
+    // epoch 0 on every word: no call uses epoch 0
+    e = cudaMemsetAsync(ctx->parts, 0, cap * sizeof(uint64_t), ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemsetAsync");
     ctx->parts_cap = cap;
   }
   if (counters > ctx->counters_cap) {
@@ -122,9 +131,18 @@ int run_decode(gla_ctx* ctx, gla::DecodeRequest& req) {
   gla::DecodePlan plan;
   int rc = gla::plan_decode(req, ctx->dev, &plan, &err);
   if (rc != GLA_OK) return fail(ctx, rc, err);
-  rc = ensure_workspace(ctx, plan.part_floats, plan.counters);
+  rc = ensure_workspace(ctx, plan.part_words, plan.counters);
   if (rc != GLA_OK) return rc;
-  rc = gla::launch_decode(req, plan, ctx->parts, ctx->counters, ctx->status, ctx->stream, &err);
+  gla::DecodeWorkspace ws;
+  ws.part = ctx->parts;
+  ws.counter = ctx->counters;
+  ws.epoch = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(ctx->status) +
+                                                    kEpochOffset);
+  ws.status = ctx->status;
+  ws.trace = (ctx->trace && (size_t)plan.grid * gla::kTraceWordsPerCta <= ctx->trace_words)
+                 ? ctx->trace
+                 : nullptr;
+  rc = gla::launch_decode(req, plan, ws, ctx->stream, &err);
   if (rc != GLA_OK) return fail(ctx, rc, err);
   return GLA_OK;
 }
@@ -267,7 +285,7 @@ int sharded(gla_ctx* ctx, int dtype, const float* q, const void* k, const void* 
             int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int64_t kv_stride,
             int32_t n_pos_local, float scale) {
   if (!ctx) return GLA_ERR_INVALID_ARG;
-  if (!ctx->comm.active())
+  if (!ctx->comm.active() && !ctx->xch.loopback())
     return fail(ctx, GLA_ERR_COMM, "gla_comm_init has not been called on this context");
   if (!xb) return fail(ctx, GLA_ERR_INVALID_ARG, "null xb");
   const size_t rec = (size_t)n_heads * (head_dim + 2);
@@ -275,7 +293,12 @@ int sharded(gla_ctx* ctx, int dtype, const float* q, const void* k, const void* 
     if (stream_capturing(ctx->stream))
       return fail(ctx, GLA_ERR_INVALID_ARG, "record buffers must grow outside stream capture");
     DeviceGuard dg(ctx->device);
-    cudaStreamSynchronize(ctx->stream);
+    std::string werr;
+    int wrc = ctx->comm.wait(ctx->stream, &werr);
+    if (wrc != GLA_OK) {
+      ctx->xch.teardown();
+      return fail(ctx, wrc, werr);
+    }
     cudaFree(ctx->records);
     cudaFree(ctx->gathered);
     ctx->records = ctx->gathered = nullptr;
@@ -342,6 +365,21 @@ int sharded(gla_ctx* ctx, int dtype, const float* q, const void* k, const void* 
   return GLA_OK;
 }
 
+// Collective end of the communicator's use before the peer exchange buffers
+// are unmapped and freed: this rank's stream drains (bounded), then every
+// rank meets at a barrier, so no rank's kernel still stores records into a
+// buffer that is about to be freed.  If a rank does not arrive within the
+// communicator timeout, the communicator is aborted (GLA_ERR_TIMEOUT) and
+// the buffers are released anyway.
+int quiesce_comm(gla_ctx* ctx) {
+  if (!ctx->comm.active()) return GLA_OK;
+  std::string err;
+  int rc = ctx->comm.wait(ctx->stream, &err);
+  if (rc == GLA_OK) rc = ctx->comm.barrier(ctx->stream, &err);
+  if (rc != GLA_OK) fail(ctx, rc, err);
+  return rc;
+}
+
 }  // namespace
 
 extern "C" {
@@ -400,8 +438,10 @@ int32_t gla_create(int32_t device, void* cuda_stream, gla_ctx** out) {
 
 int32_t gla_destroy(gla_ctx* ctx) {
   if (!ctx) return GLA_ERR_INVALID_ARG;
+  int rc = GLA_OK;
   {
     DeviceGuard dg(ctx->device);
+    rc = quiesce_comm(ctx);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     ctx->xch.teardown();
     ctx->comm.destroy();
@@ -411,9 +451,10 @@ int32_t gla_destroy(gla_ctx* ctx) {
     cudaFree(ctx->records);
     cudaFree(ctx->gathered);
     cudaFree(ctx->ingest_ws);
+    cudaFree(ctx->trace);
   }
   delete ctx;
-  return GLA_OK;
+  return rc;
 }
 
 int32_t gla_set_stream(gla_ctx* ctx, void* cuda_stream) {
@@ -427,6 +468,16 @@ const char* gla_last_error(const gla_ctx* ctx) { return ctx ? ctx->last_error.c_
 int32_t gla_device_status(gla_ctx* ctx, int32_t* device_status) {
   if (!ctx || !device_status) return GLA_ERR_INVALID_ARG;
   DeviceGuard dg(ctx->device);
+  if (ctx->comm.active()) {
+    // bounded: a collective that waits for a rank that left is ended by the
+    // host watchdog (the communicator is aborted)
+    std::string err;
+    int rc = ctx->comm.wait(ctx->stream, &err);
+    if (rc != GLA_OK) {
+      ctx->xch.teardown();
+      return fail(ctx, rc, err);
+    }
+  }
   cudaError_t e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamSynchronize");
   int32_t v = 0;
@@ -448,7 +499,8 @@ int32_t gla_reserve(gla_ctx* ctx, int32_t max_batch, int32_t max_kv_heads, int32
     return fail(ctx, GLA_ERR_INVALID_ARG, "reserve sizes must be positive");
   const int group = std::max(1, max_heads / max_kv_heads);
   DeviceGuard dg(ctx->device);
-  const size_t part = (size_t)(ctx->dev.sms + (size_t)max_batch * max_kv_heads) * group *
+  // grids run up to two CTAs an SM (batched FP16 decode)
+  const size_t part = (size_t)(2 * ctx->dev.sms + (size_t)max_batch * max_kv_heads) * group *
                       (max_head_dim + 4);
   return ensure_workspace(ctx, part, (size_t)max_batch * max_kv_heads);
 }
@@ -465,6 +517,34 @@ int32_t gla_set_option(gla_ctx* ctx, int32_t option, int32_t value) {
     case GLA_OPT_EARLY_KV_PREFETCH:
       if (value < 0 || value > 2) return fail(ctx, GLA_ERR_INVALID_ARG, "value must be 0, 1 or 2");
       ctx->opt_early_kv = value;
+      return GLA_OK;
+    case GLA_OPT_TRACE: {
+      if (value < 0 || value > 1) return fail(ctx, GLA_ERR_INVALID_ARG, "value must be 0 or 1");
+      if (value == 0) {
+        DeviceGuard dg(ctx->device);
+        cudaStreamSynchronize(ctx->stream);
+        cudaFree(ctx->trace);
+        ctx->trace = nullptr;
+        ctx->trace_words = 0;
+        return GLA_OK;
+      }
+      if (ctx->trace) return GLA_OK;
+      if (stream_capturing(ctx->stream))
+        return fail(ctx, GLA_ERR_INVALID_ARG, "turn tracing on outside stream capture");
+      DeviceGuard dg(ctx->device);
+      const size_t words = (size_t)2 * ctx->dev.sms * gla::kTraceWordsPerCta;
+      if (cudaMalloc(&ctx->trace, words * sizeof(uint64_t)) != cudaSuccess) {
+        cudaGetLastError();
+        ctx->trace = nullptr;
+        return fail(ctx, GLA_ERR_OUT_OF_MEMORY, "trace buffer allocation failed");
+      }
+      cudaMemsetAsync(ctx->trace, 0, words * sizeof(uint64_t), ctx->stream);
+      ctx->trace_words = words;
+      return GLA_OK;
+    }
+    case GLA_OPT_COMM_TIMEOUT_MS:
+      if (value < 1) return fail(ctx, GLA_ERR_INVALID_ARG, "timeout must be >= 1 ms");
+      ctx->comm.timeout_ms = value;
       return GLA_OK;
     default:
       return fail(ctx, GLA_ERR_INVALID_ARG, "unknown option");
@@ -729,6 +809,7 @@ int32_t gla_comm_init(gla_ctx* ctx, int32_t nranks, int32_t rank, const void* un
     return fail(ctx, GLA_ERR_INVALID_ARG, "bad communicator arguments");
   DeviceGuard dg(ctx->device);
   std::string err;
+  quiesce_comm(ctx);  // a previous communicator: collective end of its use
   ctx->xch.teardown();
   int rc = ctx->comm.init(nranks, rank, unique_id, &err);
   if (rc != GLA_OK) return fail(ctx, rc, err);
@@ -741,6 +822,55 @@ int32_t gla_comm_init(gla_ctx* ctx, int32_t nranks, int32_t rank, const void* un
 
 int32_t gla_comm_peer_exchange(const gla_ctx* ctx) {
   return ctx && ctx->opt_shard_exchange && ctx->xch.active() ? 1 : 0;
+}
+
+int32_t gla_comm_wait(gla_ctx* ctx) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  DeviceGuard dg(ctx->device);
+  std::string err;
+  if (!ctx->comm.active()) {
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    return e == cudaSuccess ? GLA_OK : cuda_fail(ctx, e, "cudaStreamSynchronize");
+  }
+  int rc = ctx->comm.wait(ctx->stream, &err);
+  if (rc != GLA_OK) {
+    ctx->xch.teardown();  // the communicator was aborted
+    return fail(ctx, rc, err);
+  }
+  return GLA_OK;
+}
+
+int32_t gla_comm_resync(gla_ctx* ctx) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  if (!ctx->comm.active())
+    return fail(ctx, GLA_ERR_COMM, "gla_comm_init has not been called on this context");
+  DeviceGuard dg(ctx->device);
+  std::string err;
+  // 1. every rank's stream has drained: no kernel stores records any more
+  int rc = ctx->comm.wait(ctx->stream, &err);
+  if (rc == GLA_OK) rc = ctx->comm.barrier(ctx->stream, &err);
+  // 2. records and epochs back to zero on every rank
+  if (rc == GLA_OK) rc = ctx->xch.reset(ctx->stream, &err);
+  int32_t* st = ctx->status;
+  if (rc == GLA_OK && cudaMemsetAsync(st, 0, sizeof(int32_t), ctx->stream) != cudaSuccess) {
+    cudaGetLastError();
+    rc = GLA_ERR_CUDA;
+    err = "status reset failed";
+  }
+  if (rc == GLA_OK && ctx->counters &&
+      cudaMemsetAsync(ctx->counters, 0, ctx->counters_cap * sizeof(int32_t), ctx->stream) !=
+          cudaSuccess) {
+    cudaGetLastError();
+    rc = GLA_ERR_CUDA;
+    err = "counter reset failed";
+  }
+  // 3. nobody starts a new call before every rank has reset
+  if (rc == GLA_OK) rc = ctx->comm.barrier(ctx->stream, &err);
+  if (rc != GLA_OK) {
+    if (!ctx->comm.active()) ctx->xch.teardown();
+    return fail(ctx, rc, err);
+  }
+  return GLA_OK;
 }
 
 int32_t gla_decode_sharded_f16kv(gla_ctx* ctx, const float* q, const uint16_t* k,
@@ -876,6 +1006,42 @@ int32_t gla_ingest_prompt_f16kv(gla_ctx* ctx, const float* q, const float* k, co
                        n_heads, n_kv_heads, head_dim, context_length, theta, rope_style);
 }
 
+int32_t gla_debug_advance_position(gla_ctx* ctx, int32_t* position_holder, int32_t delta,
+                                   int32_t delay_us) {
+  if (!ctx || !position_holder) return GLA_ERR_INVALID_ARG;
+  DeviceGuard dg(ctx->device);
+  std::string err;
+  int rc = gla::launch_advance_position(position_holder, delta, delay_us, ctx->stream, &err);
+  return rc == GLA_OK ? GLA_OK : fail(ctx, rc, err);
+}
+
+int32_t gla_debug_xch_loopback(gla_ctx* ctx, int32_t world) {
+  if (!ctx) return GLA_ERR_INVALID_ARG;
+  if (ctx->comm.active())
+    return fail(ctx, GLA_ERR_INVALID_ARG, "the context has a communicator");
+  DeviceGuard dg(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  if (world == 0) {
+    ctx->xch.teardown();
+    return GLA_OK;
+  }
+  std::string err;
+  int rc = ctx->xch.setup_loopback(world, &err);
+  return rc == GLA_OK ? GLA_OK : fail(ctx, rc, err);
+}
+
+int64_t gla_debug_trace(gla_ctx* ctx, uint64_t* out, int64_t capacity) {
+  if (!ctx || !out || capacity < 0) return GLA_ERR_INVALID_ARG;
+  if (!ctx->trace) return fail(ctx, GLA_ERR_INVALID_ARG, "tracing is off (GLA_OPT_TRACE)");
+  DeviceGuard dg(ctx->device);
+  cudaError_t e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamSynchronize");
+  const size_t n = std::min<size_t>((size_t)capacity, ctx->trace_words);
+  e = cudaMemcpy(out, ctx->trace, n * sizeof(uint64_t), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMemcpy");
+  return (int64_t)n;
+}
+
 int64_t gla_debug_partition(const int32_t* n_pos, int32_t n_seq, int32_t n_kv_heads, int32_t tile,
                             int32_t unit_rows, int32_t n_ctas, int32_t* cta, int32_t* seq,
                             int32_t* kv_head, int32_t* row0, int32_t* rows, int32_t* slot,
@@ -893,15 +1059,12 @@ int64_t gla_debug_partition(const int32_t* n_pos, int32_t n_seq, int32_t n_kv_he
   }
   start[n_seq] = (int32_t)(acc * n_kv_heads);
   const gla::Deal deal = gla::make_deal(start[n_seq], n_ctas, n_seq, n_kv_heads, nunits[0]);
-  // walk each CTA's range exactly as the kernel's producer and consumers do
+  // walk each CTA's tiles exactly as the kernel's producer and consumers do
   int64_t n = 0;
   for (int32_t c = 0; c < n_ctas; ++c) {
-    int32_t lo, cnt;
-    deal.range(c, &lo, &cnt);
-    gla::TileWalk wk;
-    wk.init(start.data(), nunits.data(), n_seq, lo, lo + cnt);
+    gla::CtaTiles ct = gla::cta_tiles_of(deal, c, start.data(), nunits.data(), n_seq);
     gla::Tile t;
-    while (wk.next(nunits.data(), n_seq, n_kv_heads, tile / unit_rows, unit_rows, t)) {
+    while (ct.next(nunits.data(), n_seq, n_kv_heads, tile / unit_rows, unit_rows, t)) {
       if (n >= capacity) return GLA_ERR_INVALID_ARG;
       cta[n] = c;
       seq[n] = t.b;

@@ -16,6 +16,7 @@ namespace gla {
 namespace {
 
 constexpr int kTileMax = 64;
+static_assert(kTraceWords == kTraceWordsPerCta, "trace layout shared with the context");
 static_assert(F32Consumer<128, 1>::kTileMax == kTileMax && F16Consumer<128>::kTileMax == kTileMax &&
                   Q8Consumer<128>::kTileMax == kTileMax,
               "consumers address stages with a compile-time tile height");
@@ -26,9 +27,13 @@ constexpr int kMaxStages = 8;
 
 size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 
-// LOADER 0 (tiled TMA) for one sequence whose base pointer the host knows;
-// LOADER 1 (cp.async) when the per-sequence bases live in device memory.
-int loader_for(const DecodeRequest& r) { return r.k_ptrs ? 1 : 0; }
+// LOADER 0 (tiled TMA) for one sequence whose base pointer the host knows
+// and whose kv heads each get their own CTA group (n_kv <= SMs); LOADER 1
+// (cp.async) when the per-sequence bases live in device memory, and for one
+// sequence with more kv heads than SMs (contiguous deal, base pointer a.k).
+int loader_for(const DecodeRequest& r, int sms) {
+  return (r.k_ptrs || (r.batch == 1 && r.n_kv > sms)) ? 1 : 0;
+}
 
 int esize_for(int dtype) { return dtype == GLA_DTYPE_F32 ? 4 : dtype == GLA_DTYPE_F16 ? 2 : 1; }
 
@@ -53,7 +58,7 @@ Layout layout_for(int dtype, int hd, int group, int tile, int stages, int batch,
   Layout L;
   size_t off = (size_t)stages * stage_bytes_for(dtype, hd, tile);
   L.off_bars = (int32_t)align16(off);
-  off = L.off_bars + (size_t)(stages * 2 + 1) * sizeof(uint64_t);  // full, empty, late
+  off = L.off_bars + (size_t)(stages * 3 + 2) * sizeof(uint64_t);  // full, empty, land, merge, epoch
   L.off_seq = (int32_t)align16(off);
   off = L.off_seq + (size_t)(3 * batch + 1) * sizeof(int32_t);
   L.off_q = (int32_t)align16(off);
@@ -65,7 +70,7 @@ Layout layout_for(int dtype, int hd, int group, int tile, int stages, int batch,
   L.off_merge = (int32_t)align16(off);
   off = L.off_merge + (size_t)nw * group_cap_for(dtype, group) * (hd + 4) * sizeof(float);
   L.off_flags = (int32_t)align16(off);
-  L.off_rope = (int32_t)align16(L.off_flags + 16);
+  L.off_rope = (int32_t)align16(L.off_flags + 32);
   (void)grid;
   L.total = L.off_rope + (size_t)(hd / 2) * 8 + 1024;  // + slack to 1024-align the stage ring
   return L;
@@ -217,6 +222,12 @@ int plan_decode(const DecodeRequest& r, const DeviceInfo& dev, DecodePlan* p, st
     *err = "Q8 cache: one sequence, head_dim 64 or 128";
     return GLA_ERR_NOT_SUPPORTED;
   }
+  // the tensor-map loader (fused RoPE, Q8 caches, the peer exchange) gives
+  // every kv head its own CTA group
+  if ((r.rope || r.dtype == GLA_DTYPE_Q8 || r.record_mode == 2) && r.n_kv > dev.sms) {
+    *err = "fused RoPE, Q8 caches and the peer exchange need n_kv_heads <= the SM count";
+    return GLA_ERR_NOT_SUPPORTED;
+  }
   // Work is streamed and dealt to CTAs in whole tiles of kTileMax rows.
   // (16-row units, balanced to +-16 rows per CTA, measured slower on B200
   // for every decode shape tried, 512 to 128K rows: the extra pieces and
@@ -230,7 +241,7 @@ int plan_decode(const DecodeRequest& r, const DeviceInfo& dev, DecodePlan* p, st
   }
   // The FP16 consumer with the cp.async loader (batches) runs two CTAs an SM
   // (F16Consumer::kCtasPerSm), each with half an SM's shared memory.
-  const int per_sm = (r.dtype == GLA_DTYPE_F16 && loader_for(r) == 1 && r.record_mode != 2 &&
+  const int per_sm = (r.dtype == GLA_DTYPE_F16 && loader_for(r, dev.sms) == 1 && r.record_mode != 2 &&
                       dev.smem_per_sm > 0)
                          ? 2
                          : 1;
@@ -241,6 +252,8 @@ int plan_decode(const DecodeRequest& r, const DeviceInfo& dev, DecodePlan* p, st
   int grid = dev.sms * per_sm;
   if (r.n_pos_dev == nullptr) grid = (int)std::min<int64_t>(grid, W);
   grid = std::max(grid, 1);
+  // the tensor-map loader's round-robin deal gives every kv head a CTA group
+  if (loader_for(r, dev.sms) == 0) grid = std::max(grid, r.n_kv);
   // Stages: as many as fit (the ring is the only large smem consumer).
   int stages = kMaxStages;
   Layout L = layout_for(r.dtype, hd, group, tile, stages, r.batch, grid);
@@ -252,21 +265,22 @@ int plan_decode(const DecodeRequest& r, const DeviceInfo& dev, DecodePlan* p, st
     *err = "shared memory layout does not fit";
     return GLA_ERR_NOT_SUPPORTED;
   }
+  p->loader = loader_for(r, dev.sms);
   p->tile = tile;
   p->stages = stages;
   p->grid = grid;
   p->threads = (nw_for(r.dtype) + 1) * 32;
   p->smem = L.total;
-  p->part_floats = (size_t)(grid + r.batch * r.n_kv) * group * (hd + 4);
+  p->part_words = (size_t)(grid + r.batch * r.n_kv) * group * (hd + 4);
   p->counters = (size_t)r.batch * r.n_kv;
   return GLA_OK;
 }
 
-int launch_decode(const DecodeRequest& r, const DecodePlan& p, float* ws_part, int32_t* ws_counter,
-                  int32_t* status, cudaStream_t stream, std::string* err) {
+int launch_decode(const DecodeRequest& r, const DecodePlan& p, const DecodeWorkspace& ws,
+                  cudaStream_t stream, std::string* err) {
   const int hd = r.head_dim;
   const int group = r.n_heads / r.n_kv;
-  const int loader = loader_for(r);
+  const int loader = p.loader;
   Layout L = layout_for(r.dtype, hd, group, p.tile, p.stages, r.batch, p.grid);
   DecodeArgs a{};
   if (loader == 0) {
@@ -302,9 +316,12 @@ int launch_decode(const DecodeRequest& r, const DecodePlan& p, float* ws_part, i
   a.xch_out = r.xch_out;
   a.xch_world = r.xch_world;
   a.xch_rank = r.xch_rank;
-  a.ws_part = ws_part;
-  a.ws_counter = ws_counter;
-  a.status = status;
+  a.ws_part = ws.part;
+  a.ws_counter = ws.counter;
+  a.ws_epoch = ws.epoch;
+  a.status = ws.status;
+  a.trace = ws.trace;
+  a.scales = r.scales;
   a.stage_bytes = (int32_t)stage_bytes_for(r.dtype, hd, p.tile);
   a.off_bars = L.off_bars;
   a.off_seq = L.off_seq;

@@ -94,9 +94,12 @@ struct DecodeArgs {
   double rope_theta;
   int32_t rope;
   int32_t rope_style;
-  float* ws_part;              // workspace slots [P + B*n_kv][G][HD+4] (o, m, l, pad)
-  int32_t* ws_counter;         // [B*n_kv], zero between calls
+  uint64_t* ws_part;           // piece slots [P + B*n_kv][G][HD+4] tagged words (o, m, l, pad)
+  int32_t* ws_counter;         // [B*n_kv] piece counters, zero between calls
+  unsigned long long* ws_epoch;  // call epoch << 32 | CTAs that took a ticket this call
   int32_t* status;             // device status word
+  uint64_t* trace;             // optional [grid][kTraceWords] phase stamps (null: off)
+  const void* scales;          // Q8 cache: [rows][n_kv][8] halves (row patches)
   // shared memory layout (bytes)
   int32_t stage_bytes;         // 2 * tile * head_dim * element size
   int32_t off_bars;
@@ -848,6 +851,26 @@ __device__ __forceinline__ void write_final4(const DecodeArgs& a, int b, int hq,
 }
 
 // ---------------------------------------------------------------------------
+// Phase trace (DecodeArgs::trace, off when null): %globaltimer stamps per CTA,
+// kTraceWords words a CTA, overwritten by every launch.
+// ---------------------------------------------------------------------------
+constexpr int kTraceWords = 16;
+enum TraceSlot : int {
+  kTrEntry = 0,      // kernel entry
+  kTrWait = 1,       // dependency wait returned
+  kTrQ = 2,          // q of the first piece in shared memory
+  kTrFirstTile = 3,  // first tile ready for the consumers
+  kTrLastTile = 4,   // last tile consumed
+  kTrCounted = 5,    // piece stored and counted (or final, one-piece segment)
+  kTrMerged = 6,     // merger: segment merged and written
+  kTrPublished = 7,  // merger, sharded: every rank's records merged into xb
+  kTrProdFirst = 8,  // producer: early copies forwarded, first copy after the wait issued
+  kTrProdLast = 9,   // producer: last copy issued
+  kTrInfo = 10,      // tiles | early tiles << 16 | merger << 24 | smid << 32
+  kTrExit = 11,      // consumers done
+};
+
+// ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
 template <int HD, class Consumer, int LOADER, bool XCH>
@@ -865,35 +888,81 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int B = a.batch, n_kv = a.n_kv, G = a.group;
   const int unit_rows = a.tile;  // work units are whole tiles
-  constexpr int tile_units = 1;
+  const int32_t P = (int32_t)gridDim.x;
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bars);
   uint64_t* empty = full + a.stages;
-  uint64_t* late_bar = empty + a.stages;  // fused RoPE: the newest-row tile's early copy
+  uint64_t* land = empty + a.stages;  // early copies (issued before the dependency wait)
+  uint64_t* mbar = land + a.stages;   // piece gathers of the merge
+  uint64_t* ep_bar = mbar + 1;        // the call epoch is in flags[4]
   int32_t* seq_start = reinterpret_cast<int32_t*>(smem + a.off_seq);  // [B+1] (units)
   int32_t* nunits = seq_start + (B + 1);                              // [B]
   int32_t* npos = nunits + B;                                         // [B]
   float* qs = reinterpret_cast<float*>(smem + a.off_q);                // [kMaxGroup][HD]
   float* pbuf = reinterpret_cast<float*>(smem + a.off_pbuf);           // [NW][kPbufFloats]
   float* merge = reinterpret_cast<float*>(smem + a.off_merge);         // [NW][kMG][HD+4]
-  volatile int* flags = reinterpret_cast<volatile int*>(smem + a.off_flags);  // [0]=abort [1]=last
+  // [0] abort  [1] this CTA merges  [2] exchange epoch  [3] position hint
+  // [4] call epoch  [5] early copies issued  [6] first tile stamped
+  volatile int* flags = reinterpret_cast<volatile int*>(smem + a.off_flags);
   float2* rope_cs = reinterpret_cast<float2*>(smem + a.off_rope);      // [HD/2] (fused RoPE)
+  // phase stamps (a.trace lives in the parameter bank: no register stays live)
+  auto stamp = [&](int slot) {
+    if (a.trace) a.trace[(size_t)blockIdx.x * kTraceWords + slot] = global_timer_ns();
+  };
+
+  // The deal's mode does not depend on the lengths (see make_deal).  The
+  // tensor-map loader serves one sequence with n_kv <= P only (the host plans
+  // other single-sequence calls on the cp.async loader): always round robin.
+  if (LOADER == 0 && (B != 1 || n_kv > P)) {
+    if (threadIdx.x == 0) atomicCAS(a.status, 0, GLA_ERR_NOT_SUPPORTED);
+    return;
+  }
+  const bool mode1 = LOADER == 0 || (B == 1 && n_kv <= P);
+  // Early KV prefetch (programmatic dependent launch): the producer starts
+  // streaming this CTA's first tiles while the preceding kernel on the stream
+  // drains.  Which tiles a CTA owns depends on the length only through their
+  // count (round robin), so the count comes from a hint: the host n_pos, or
+  // (level 2) the device position read before the wait, which may be stale.
+  // Every early copy lands on its own barrier land[k]; after the wait the
+  // producer drops the copies the true length does not need, rewrites in
+  // shared memory the two newest rows [n_pos - 2, n_pos) of the tiles it
+  // keeps (the rows a preceding kernel may still have been writing: a KV
+  // append at n_pos - 1, the previous token's fused append at n_pos - 2),
+  // and hands each kept stage to the consumers.  Everything else a preceding
+  // kernel writes (q, the positions, the workspace) is read after the wait.
+  const bool early = LOADER == 0 && a.early_kv >= 1 &&
+                     (a.n_pos_dev == nullptr || (a.early_kv >= 2 && mode1));
 
   if (tid == 0) {
+    stamp(kTrEntry);
     for (int s = 0; s < a.stages; ++s) {
       mbar_init(&full[s], LOADER == 0 ? 1 : 32);
       mbar_init(&empty[s], NW);
+      mbar_init(&land[s], 1);
     }
-    mbar_init(late_bar, 1);
+    mbar_init(mbar, 1);
+    mbar_init(ep_bar, 1);
     flags[0] = 0;
     flags[1] = 0;
     flags[2] = 0;
+    flags[4] = 0;
+    flags[6] = 0;
+    int32_t hint = 0;
+    if (early) {
+      hint = a.n_pos_dev ? ld_relaxed_gpu_s32(a.n_pos_dev) + a.n_pos_add : a.n_pos;
+      hint = hint < 0 ? 0 : (hint > a.n_pos_cap ? a.n_pos_cap : hint);
+    }
+    flags[3] = hint;
+    flags[5] = 0;
     fence_mbarrier_init();
   }
   if (LOADER == 0 && warp == NW && lane == 0) {
     prefetch_tmap(&a.tmap_k);
     prefetch_tmap(&a.tmap_v);
   }
+  __syncthreads();
+  const int32_t hint = flags[3];
+
   // per-sequence rows and unit prefix (warp 0 scans 32 sequences at a time)
   auto scan_sequences = [&]() {
     if (warp == 0) {
@@ -924,25 +993,18 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
       if (lane == 0) seq_start[B] = carry * n_kv;
     }
   };
-  // Fused RoPE: (cos, sin) of every pair at the new position (row n_pos - 1
-  // of the one sequence), computed once per CTA.
-  auto rope_table = [&]() {
-    if (!a.rope) return;
-    const int pos = npos[0] - 1;
+  // Fused RoPE: (cos, sin) of every pair at position `pos`, once per CTA.
+  auto rope_table = [&](int pos) {
     for (int i = tid; i < HD / 2; i += blockDim.x) {
       float c, sn;
       rope_cos_sin(pos, i, HD, a.rope_theta, &c, &sn);
       rope_cs[i] = make_float2(c, sn);
     }
   };
-  // Fused RoPE + append, producer warp: kv head g's new key row (rotated)
-  // and value row are written at row n_pos - 1 of the caches, then a proxy
-  // fence orders those generic stores before the tensor copy that reads the
-  // row back (only the CTA holding that row's tile does this).
-  // Fused RoPE, early-prefetched newest-row tile (stage st, row r of the
+  // Fused RoPE, newest row staged in shared memory (stage st, row r of the
   // tile): the producer warp writes kv head g's rotated key row and value row
   // to the caches (for later calls) and over the stale row of the staged tile
-  // (128B-swizzled FP32 layout), after the stage's early copy has landed.
+  // (128B-swizzled FP32 layout), after the stage's copy has landed.
   auto append_row_stage = [&](int g, int st, int r) {
     if constexpr (Consumer::kElemBytes != 4) return;  // fused RoPE writes FP32 caches only
     const int pos = npos[0] - 1;
@@ -974,6 +1036,10 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
       *at(vs, i1) = v1;
     }
   };
+  // Fused RoPE + append, producer warp, before a copy issued after the wait
+  // reads row n_pos - 1: kv head g's rotated key row and its value row are
+  // written there, then a proxy fence orders those generic stores before the
+  // tensor copy that reads the row back.
   auto append_row = [&](int g) {
     if constexpr (Consumer::kElemBytes != 4) return;  // fused RoPE writes FP32 caches only
     const int pos = npos[0] - 1;
@@ -997,13 +1063,51 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
     asm volatile("fence.proxy.async.global;" ::: "memory");
     __syncwarp();
   };
+  // Producer warp, after the wait: cache row `row` of kv head g (K, V and, for
+  // a Q8 cache, the scale row) re-read from global memory into row r of the
+  // tile staged in stage st.
+  auto copy_row_to_stage = [&](int st, int g, int row, int r) {
+    if constexpr (LOADER == 0) {
+      char* ks = smem + (size_t)st * a.stage_bytes;
+      char* vs = ks + (size_t)a.tile * HD * esize;
+      const int64_t off = ((int64_t)row * a.kv_stride + (int64_t)g * HD) * esize;
+      const char* kg = static_cast<const char*>(a.k) + off;
+      const char* vg = static_cast<const char*>(a.v) + off;
+      constexpr int kCpr = HD * esize / 16;  // 16-byte chunks per row
+      uint4 x[(2 * kCpr + 31) / 32];
+#pragma unroll
+      for (int u = 0; u < (2 * kCpr + 31) / 32; ++u) {
+        const int c = lane + 32 * u;
+        if (c < 2 * kCpr) {
+          const int cc = c < kCpr ? c : c - kCpr;
+          x[u] = __ldcg(reinterpret_cast<const uint4*>((c < kCpr ? kg : vg) + cc * 16));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < (2 * kCpr + 31) / 32; ++u) {
+        const int c = lane + 32 * u;
+        if (c < 2 * kCpr) {
+          const int cc = c < kCpr ? c : c - kCpr;
+          *reinterpret_cast<uint4*>((c < kCpr ? ks : vs) + TL::chunk_off(a.tile, r, cc * (16 / esize))) =
+              x[u];
+        }
+      }
+      if constexpr (Consumer::kQ8) {
+        if (lane == 0) {
+          const char* sg = static_cast<const char*>(a.scales) +
+                           ((int64_t)row * n_kv + g) * kQ8ScaleRowBytes;
+          *reinterpret_cast<uint4*>(ks + (size_t)2 * a.tile * HD + r * kQ8ScaleRowBytes) =
+              __ldcg(reinterpret_cast<const uint4*>(sg));
+        }
+      }
+    }
+  };
   // TMA loads of one tile (LOADER 0): whole boxes of `tile` rows; rows past
   // the tensor map's extent are zero-filled, so the byte count is the boxes'
   // size.  Rows past n_pos inside the extent are loaded and masked later.
-  auto tma_tile = [&](int st, const Tile& t, uint64_t pol, uint64_t* bar = nullptr) {
+  auto tma_tile = [&](int st, const Tile& t, uint64_t pol, uint64_t* bar) {
     char* ks = smem + (size_t)st * a.stage_bytes;
     char* vs = ks + (size_t)a.tile * HD * esize;
-    if (bar == nullptr) bar = &full[st];
     mbar_arrive_expect_tx(bar, (uint32_t)(2 * a.tile * HD * esize +
                                           (Consumer::kQ8 ? a.tile * kQ8ScaleRowBytes : 0)));
 #pragma unroll
@@ -1018,143 +1122,136 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
       tma_load_2d(ks + (size_t)2 * a.tile * HD, &a.tmap_s, t.g * kQ8ScaleHalves, t.row0,
                   bar, pol);
   };
-  // Early KV prefetch (programmatic dependent launch).  The work partition
-  // needs only the positions, so the producer may start streaming this CTA's
-  // first tiles while the preceding kernel on the stream drains: with a host
-  // n_pos (early_kv >= 1), or with positions read from the device
-  // (early_kv == 2: the caller vouches that a kernel releasing its
-  // dependents early does not write them).  Only tiles holding cache history
-  // (rows < n_pos - 1) are fetched early: the newest row is the one a KV
-  // append kernel may have just written.  Decode kernels (the only kernels
-  // here that release dependents early) never write a cache or a position; a
-  // preceding kernel that does not release dependents has finished before
-  // this grid starts.
-  // The ring's first pass (up to `stages` tiles) is walked here; a tile
-  // holding a sequence's newest row is skipped (bit k of `late`) and fetched
-  // after the wait, the tiles behind it are not held back.
-  const bool early = LOADER == 0 && (a.n_pos_dev == nullptr ? a.early_kv >= 1 : a.early_kv >= 2);
-  int32_t n_early = 0;
-  uint32_t late = 0;
+
+  // ---------------- early copies (before the dependency wait) ----------------
+  int32_t n_early = 0;  // producer warp: the ring's first pass, copied early
   if (early) {
-    scan_sequences();
-    __syncthreads();
-    rope_table();  // the position is known: overlap the double-precision work too
-    if (warp == NW && lane == 0) {
-      const Deal d0 = make_deal(seq_start[B], (int32_t)gridDim.x, B, n_kv, nunits[0]);
-      int32_t lo, cnt;
-      d0.range(blockIdx.x, &lo, &cnt);
+    if (a.rope) rope_table(hint - 1);  // recomputed after the wait if the position moved
+    if (warp == NW) {
       const uint64_t pol = l2_evict_first_policy();
-      TileWalk wk;
-      wk.init(seq_start, nunits, B, lo, lo + cnt);
+      const int32_t nu_h = ceil_div(hint, unit_rows);
+      int32_t ss[2] = {0, n_kv * nu_h}, nus[1] = {nu_h};
+      CtaTiles ct = cta_tiles_of(make_deal(ss[1], P, 1, n_kv, nu_h), blockIdx.x, ss, nus, 1);
       Tile t;
       int32_t seg = -1;
-      while (n_early < a.stages && wk.next(nunits, B, n_kv, tile_units, unit_rows, t)) {
-        // fused RoPE: warm L2 with the inputs read right after the wait (the
-        // group's q vectors, the new key and value rows of kv head g)
-        if (a.rope && t.b * n_kv + t.g != seg) {
-          seg = t.b * n_kv + t.g;
-          prefetch_l2_bulk(a.q + ((int64_t)t.b * a.n_heads + (int64_t)t.g * G) * HD,
-                           (uint32_t)(G * HD * sizeof(float)));
-          prefetch_l2_bulk(a.rope_k + (int64_t)t.g * HD, (uint32_t)(HD * sizeof(float)));
-          prefetch_l2_bulk(a.rope_v + (int64_t)t.g * HD, (uint32_t)(HD * sizeof(float)));
-        }
-        if (t.row0 + t.units * unit_rows >= npos[t.b]) {  // newest row
-          late |= 1u << n_early;
-          // fused RoPE: fetch the tile now (its newest row is stale) and
-          // overwrite that row in shared memory after the wait
-          if (a.rope) tma_tile(n_early, t, pol, late_bar);
-        } else {
-          tma_tile(n_early, t, pol);
+      while (n_early < a.stages && ct.next(nus, 1, n_kv, 1, unit_rows, t)) {
+        if (lane == 0) {
+          // fused RoPE: warm L2 with the inputs read right after the wait (the
+          // group's q vectors, the new key and value rows of kv head g)
+          if (a.rope && t.g != seg) {
+            seg = t.g;
+            prefetch_l2_bulk(a.q + (int64_t)t.g * G * HD, (uint32_t)(G * HD * sizeof(float)));
+            prefetch_l2_bulk(a.rope_k + (int64_t)t.g * HD, (uint32_t)(HD * sizeof(float)));
+            prefetch_l2_bulk(a.rope_v + (int64_t)t.g * HD, (uint32_t)(HD * sizeof(float)));
+          }
+          tma_tile(n_early, t, pol, &land[n_early]);
         }
         ++n_early;
       }
+      if (lane == 0) flags[5] = n_early;
     }
   }
   // Nothing below may read memory a preceding kernel writes (n_pos, q, the
   // newest cache rows, the workspace) before that kernel has completed.
   pdl_wait();
   pdl_launch_dependents();
-  if (!early) scan_sequences();
+  if (tid == 0) stamp(kTrWait);
+  scan_sequences();
   __syncthreads();
-  if (!early && a.rope) {
-    rope_table();
+  if (a.rope && (!early || npos[0] != hint)) {
+    rope_table(npos[0] - 1);
     __syncthreads();
   }
 
   const int32_t W = seq_start[B];
-  const Deal deal = make_deal(W, (int32_t)gridDim.x, B, n_kv, nunits[0]);
-  int32_t my_lo, my_count;
-  deal.range(blockIdx.x, &my_lo, &my_count);
+  const Deal deal = make_deal(W, P, B, n_kv, nunits[0]);
+  auto cta_tiles = [&]() { return cta_tiles_of(deal, blockIdx.x, seq_start, nunits, B); };
 
   if (warp == NW) {
     // ---------------- producer ----------------
-    if (my_count > 0) {
-      const uint64_t pol = l2_evict_first_policy();
-      const int32_t first = early ? __shfl_sync(0xffffffffu, n_early, 0) : 0;
-      const uint32_t late_mask = early ? __shfl_sync(0xffffffffu, late, 0) : 0u;
-      TileWalk wk;
-      wk.init(seq_start, nunits, B, my_lo, my_lo + my_count);
-      Tile t;
-      for (int32_t k = 0; k < first; ++k) {  // first ring pass: no empty-barrier waits
-        wk.next(nunits, B, n_kv, tile_units, unit_rows, t);
-        if ((late_mask >> k) & 1u) {
-          if (a.rope) {
-            bool landed = true;
-            if (lane == 0) landed = mbar_wait(late_bar, 0, flags, a.status);
-            landed = __shfl_sync(0xffffffffu, landed, 0);
-            if (landed) append_row_stage(t.g, k, npos[0] - 1 - t.row0);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&full[k]);  // the stage's only arrival this pass
-          } else if (lane == 0) {
-            tma_tile(k, t, pol);
-          }
+    // The call's epoch (tags of the piece words): every CTA takes a ticket
+    // from the workspace's epoch word (epoch << 32 | CTAs of this call so
+    // far); the last CTA to take one moves the word to the next epoch.  All
+    // CTAs of a call see the same epoch, every call a larger one.  Lane 31
+    // takes it and settles it after the copies are issued, when the result
+    // has long arrived; the consumers read it behind ep_bar.
+    unsigned long long ticket = 0;
+    if (lane == 31) ticket = atomicAdd(a.ws_epoch, 1ull);
+    const uint64_t pol = l2_evict_first_policy();
+    CtaTiles ct = cta_tiles();
+    Tile t;
+    // the early copies: keep (rewrite the newest rows, hand to the
+    // consumers) or drop; every one is waited for, so no copy is still in
+    // flight when the CTA exits
+    for (int32_t k = 0; k < n_early; ++k) {
+      const bool keep = ct.next(nunits, B, n_kv, 1, unit_rows, t);
+      bool landed = true;
+      if (lane == 0) landed = mbar_wait(&land[k], 0, flags, a.status);
+      landed = __shfl_sync(0xffffffffu, landed, 0);
+      if (!keep) continue;
+      if (landed) {
+        const int np = npos[t.b];
+        const int r_hi = imin(t.row0 + unit_rows, np);
+        for (int r = (t.row0 > np - 2 ? t.row0 : np - 2); r < r_hi; ++r) {
+          if (a.rope && r == np - 1) append_row_stage(t.g, k, r - t.row0);
+          else copy_row_to_stage(k, t.g, r, r - t.row0);
         }
       }
       __syncwarp();
-      int cur_b = -1;
-      const char* kb = nullptr;
-      const char* vb = nullptr;
-      int st = first % a.stages;
-      uint32_t phase = first < a.stages ? 1u : 0u;  // empty-barrier parity of the ring pass
-      for (; wk.next(nunits, B, n_kv, tile_units, unit_rows, t);) {
-        if (!mbar_wait(&empty[st], phase, flags, a.status)) break;
-        if constexpr (LOADER == 0) {
-          if (a.rope && t.row0 + t.units * unit_rows >= npos[t.b]) append_row(t.g);
-          if (lane == 0) tma_tile(st, t, pol);
-          __syncwarp();
-        } else {
-          if (t.b != cur_b) {
-            cur_b = t.b;
-            kb = static_cast<const char*>(a.k_ptrs ? a.k_ptrs[cur_b] : a.k);
-            vb = static_cast<const char*>(a.v_ptrs ? a.v_ptrs[cur_b] : a.v);
-            // caller-supplied device pointers: a null or unaligned base would
-            // make the copies fault, so refuse it and drain instead
-            if (kb == nullptr || vb == nullptr ||
-                ((reinterpret_cast<uintptr_t>(kb) | reinterpret_cast<uintptr_t>(vb)) & 15u)) {
-              atomicCAS(a.status, 0, GLA_ERR_ALIGNMENT);
-              flags[0] = 1;
-              break;
-            }
+      if (lane == 0) mbar_arrive(&full[k]);  // the stage's only arrival this pass
+    }
+    if (lane == 0) stamp(kTrProdFirst);
+    int cur_b = -1;
+    const char* kb = nullptr;
+    const char* vb = nullptr;
+    int st = n_early % a.stages;
+    uint32_t phase = n_early < a.stages ? 1u : 0u;  // empty-barrier parity of the ring pass
+    for (; ct.next(nunits, B, n_kv, 1, unit_rows, t);) {
+      if (!mbar_wait(&empty[st], phase, flags, a.status)) break;
+      if constexpr (LOADER == 0) {
+        if (a.rope && t.row0 + t.units * unit_rows >= npos[t.b]) append_row(t.g);
+        if (lane == 0) tma_tile(st, t, pol, &full[st]);
+        __syncwarp();
+      } else {
+        if (t.b != cur_b) {
+          cur_b = t.b;
+          kb = static_cast<const char*>(a.k_ptrs ? a.k_ptrs[cur_b] : a.k);
+          vb = static_cast<const char*>(a.v_ptrs ? a.v_ptrs[cur_b] : a.v);
+          // caller-supplied device pointers: a null or unaligned base would
+          // make the copies fault, so refuse it and drain instead
+          if (kb == nullptr || vb == nullptr ||
+              ((reinterpret_cast<uintptr_t>(kb) | reinterpret_cast<uintptr_t>(vb)) & 15u)) {
+            atomicCAS(a.status, 0, GLA_ERR_ALIGNMENT);
+            flags[0] = 1;
+            break;
           }
-          char* ks = smem + (size_t)st * a.stage_bytes;
-          char* vs = ks + (size_t)a.tile * HD * esize;
-          const int rows = imin(t.units * unit_rows, npos[t.b] - t.row0);
-          constexpr int kCpr = HD * esize / 16;  // 16-byte chunks per row
-          for (int idx = lane; idx < rows * kCpr; idx += 32) {
-            const int r = idx / kCpr, c = idx - r * kCpr;
-            const int64_t off =
-                ((int64_t)(t.row0 + r) * a.kv_stride + (int64_t)t.g * HD) * esize + c * 16;
-            const int soff = TL::chunk_off(a.tile, r, c * (16 / esize));
-            cp_async_16(ks + soff, kb + off, pol);
-            cp_async_16(vs + soff, vb + off, pol);
-          }
-          cp_async_arrive_noinc(&full[st]);
         }
-        if (++st == a.stages) {
-          st = 0;
-          phase ^= 1u;
+        char* ks = smem + (size_t)st * a.stage_bytes;
+        char* vs = ks + (size_t)a.tile * HD * esize;
+        const int rows = imin(t.units * unit_rows, npos[t.b] - t.row0);
+        constexpr int kCpr = HD * esize / 16;  // 16-byte chunks per row
+        for (int idx = lane; idx < rows * kCpr; idx += 32) {
+          const int r = idx / kCpr, c = idx - r * kCpr;
+          const int64_t off =
+              ((int64_t)(t.row0 + r) * a.kv_stride + (int64_t)t.g * HD) * esize + c * 16;
+          const int soff = TL::chunk_off(a.tile, r, c * (16 / esize));
+          cp_async_16(ks + soff, kb + off, pol);
+          cp_async_16(vs + soff, vb + off, pol);
         }
+        cp_async_arrive_noinc(&full[st]);
       }
+      if (++st == a.stages) {
+        st = 0;
+        phase ^= 1u;
+      }
+    }
+    if (lane == 0) stamp(kTrProdLast);
+    if (lane == 31) {
+      const uint32_t call_ep = (uint32_t)(ticket >> 32) + 1u;
+      flags[4] = (int)call_ep;
+      if ((uint32_t)ticket == (uint32_t)P - 1u)
+        atomicExch(a.ws_epoch, (unsigned long long)call_ep << 32);
+      mbar_arrive(ep_bar);
     }
     return;
   }
@@ -1250,13 +1347,17 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
       if constexpr (XCH) publish_merge(g);
     }
   }
-  if (my_count == 0) return;
+  const CtaTiles ct = cta_tiles();
+  const int my_tiles = ct.count;
+  if (my_tiles == 0) return;
 
   Consumer cons;
   float* pbuf_w = pbuf + warp * Consumer::kPbufFloats;
   constexpr int kMH = merge_head_floats<HD>();
   float* merge_w = merge + warp * kMG * kMH;
-  constexpr int kSH = slot_head_floats<HD>();
+  constexpr int kSH = slot_head_floats<HD>();  // words per head in a piece slot
+  constexpr int kMergeBytes = NW * kMG * kMH * (int)sizeof(float);  // the warp merge buffer
+  uint32_t gather_phase = 0;  // completed phases of the merge barrier
 
   // The group's q vectors, pre-scaled by scale*log2(e), rows >= G zeroed.
   auto load_q = [&](int b, int g) {
@@ -1293,84 +1394,188 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
     consumer_sync(kNCT);
   };
 
-  // Merges the pieces of segment (b, g) held in workspace slots c + s for
-  // c in [c0, c0 + npieces).  An item is (head, 4 columns); tpi adjacent
-  // threads share an item (as many as fill the consumer threads), each
-  // folding every tpi-th piece in with a running log-sum-exp, 16 pieces per
-  // round of loads (one round up to 16 * tpi pieces); shuffles then join the
-  // tpi partial results.  No shared memory and no barrier.
-  auto combine_pieces = [&](int b, int g, int s, int c0, int npieces) {
-    constexpr int kD4 = HD / 4;
+  // ---- split-KV merge ------------------------------------------------------
+  // Every piece word is 64 bits: (float bits, call epoch << 32), stored with
+  // one single-copy-atomic access, so the merger recognises the current
+  // call's words by their epoch and needs no fence between a piece's stores
+  // and the segment counter (a relaxed add).  Epochs grow with every call on
+  // the workspace, whatever its shape, so a slot word left by any earlier
+  // call never carries the current epoch.
+  auto tag = [](float v, uint32_t ep) -> uint64_t {
+    return (uint64_t)__float_as_uint(v) | ((uint64_t)ep << 32);
+  };
+  auto fresh = [](uint64_t w, uint32_t ep) { return (uint32_t)(w >> 32) == ep; };
+  // Piece words of head h, columns d..d+3 (o), and (m, l) polled from global
+  // memory until they carry epoch ep (bounded).
+  auto poll_piece = [&](const uint64_t* row, int d, uint32_t ep, uint64_t (&w)[6]) {
+    unsigned long long t0 = 0;
+    for (;;) {
+      ld_relaxed_gpu_u64x2(row + d, w[0], w[1]);
+      ld_relaxed_gpu_u64x2(row + d + 2, w[2], w[3]);
+      ld_relaxed_gpu_u64x2(row + HD, w[4], w[5]);
+      bool ok = true;
+#pragma unroll
+      for (int e = 0; e < 6; ++e) ok = ok && fresh(w[e], ep);
+      if (ok || flags[0]) return;
+      if (t0 == 0) {
+        t0 = global_timer_ns();
+      } else if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+        flags[0] = 1;
+        atomicCAS(a.status, 0, GLA_ERR_TIMEOUT);
+        return;
+      }
+    }
+  };
+  // Running log-sum-exp fold of one piece (log2-domain m) into (O, M, L).
+  auto fold = [&](float4& O, float& M, float& L, const uint64_t (&w)[6]) {
+    const float m = __uint_as_float((uint32_t)w[4]);
+    if (m == -INFINITY) return;  // an empty piece
+    const float l = __uint_as_float((uint32_t)w[5]);
+    const float Mn = fmaxf(M, m);
+    const float sa = (M == -INFINITY) ? 0.f : fast_exp2(M - Mn);
+    const float sb = fast_exp2(m - Mn);
+    O.x = O.x * sa + sb * __uint_as_float((uint32_t)w[0]);
+    O.y = O.y * sa + sb * __uint_as_float((uint32_t)w[1]);
+    O.z = O.z * sa + sb * __uint_as_float((uint32_t)w[2]);
+    O.w = O.w * sa + sb * __uint_as_float((uint32_t)w[3]);
+    L = L * sa + sb * l;
+    M = Mn;
+  };
+  auto join = [&](float4& O, float& M, float& L, int tpi) {
+    for (int off = 1; off < tpi; off <<= 1) {
+      const float Mo = __shfl_xor_sync(0xffffffffu, M, off);
+      const float Lo = __shfl_xor_sync(0xffffffffu, L, off);
+      float4 Oo;
+      Oo.x = __shfl_xor_sync(0xffffffffu, O.x, off);
+      Oo.y = __shfl_xor_sync(0xffffffffu, O.y, off);
+      Oo.z = __shfl_xor_sync(0xffffffffu, O.z, off);
+      Oo.w = __shfl_xor_sync(0xffffffffu, O.w, off);
+      const float Mn = fmaxf(M, Mo);
+      const float sa = (M == -INFINITY) ? 0.f : fast_exp2(M - Mn);
+      const float sb = (Mo == -INFINITY) ? 0.f : fast_exp2(Mo - Mn);
+      O.x = O.x * sa + Oo.x * sb; O.y = O.y * sa + Oo.y * sb;
+      O.z = O.z * sa + Oo.z * sb; O.w = O.w * sa + Oo.w * sb;
+      L = L * sa + Lo * sb;
+      M = Mn;
+    }
+  };
+  // Items (head, 4 columns) of the merge and the threads that share one.
+  constexpr int kD4 = HD / 4;
+  constexpr int kIPT = (kMaxGroup * kD4 + kNCT - 1) / kNCT;  // item passes a thread
+  auto merge_shape = [&](int* tpi) {
     const int items = G * kD4;
-    int tpi = 1;
-    while (tpi < 8 && items * tpi * 2 <= kNCT) tpi *= 2;
-    const int64_t step = (int64_t)G * kSH;
-    for (int base = 0; base < items * tpi; base += kNCT) {  // warp-uniform trip count
-      const int idx = base + tid;
+    int t = 1;
+    while (t < 8 && items * t * 2 <= kNCT) t *= 2;
+    *tpi = t;
+    return items;
+  };
+
+  // Merger: the segment's slots c0 + s .. c0 + s + npieces - 1 (consecutive)
+  // are bulk-copied into shared memory `dst` (the drained ring, or the warp
+  // merge buffer when the ring still holds this CTA's next piece) in chunks
+  // of whole pieces; every thread folds its items' pieces from there (words
+  // of another call are polled again from global memory).
+  auto gather = [&](int b, int g, int s, int c0, int npieces, uint32_t ep, char* dst_bytes,
+                    int cap_bytes) {
+    int tpi;
+    const int items = merge_shape(&tpi);
+    const int piece_words = G * kSH;
+    const uint64_t* src0 = a.ws_part + (int64_t)(c0 + s) * piece_words;
+    const int cap = imin(npieces, cap_bytes / (piece_words * 8));
+    uint64_t* dst = reinterpret_cast<uint64_t*>(dst_bytes);
+    // early copies that the true length did not need may still be landing in
+    // the ring: the producer drains them, and so does the merger before it
+    // overwrites the ring
+    if (tid == 0 && dst_bytes == smem)
+      for (int k = my_tiles; k < flags[5]; ++k) mbar_wait(&land[k], 0, flags, a.status);
+    auto copy_chunk = [&](int p0, int n) {
+      if (tid == 0) {
+        fence_proxy_async_global();  // this CTA's own piece stores, before the copy
+        const uint32_t bytes = (uint32_t)(n * piece_words * 8);
+        mbar_arrive_expect_tx(mbar, bytes);
+        bulk_g2s_plain(dst, src0 + (int64_t)p0 * piece_words, bytes, mbar);
+      }
+      mbar_wait(mbar, (uint32_t)(gather_phase++ & 1), flags, a.status);
+    };
+    // folds pieces [p0, p0 + n) of the shared-memory chunk into item idx's state
+    auto fold_chunk = [&](int idx, int p0, int n, float4& O, float& M, float& L) {
       const bool active = idx < items * tpi;
       const int it = active ? idx / tpi : 0, j = idx % tpi;
       const int h = it / kD4, d = (it - h * kD4) * 4;
-      const float* sbase = a.ws_part + ((int64_t)(c0 + s) * G + h) * kSH;
-      float M = -INFINITY, L = 0.f;
-      float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int c = active ? j : npieces; c < npieces; c += 16 * tpi) {
-        float4 v[16];
-        float2 ml[16];
+      if (!active) return;
+      for (int pi = j; pi < n; pi += tpi) {
+        const uint64_t* row = dst + ((int64_t)pi * G + h) * kSH;
+        uint64_t w[6];
+        const ulonglong2 w01 = *reinterpret_cast<const ulonglong2*>(row + d);
+        const ulonglong2 w23 = *reinterpret_cast<const ulonglong2*>(row + d + 2);
+        const ulonglong2 w45 = *reinterpret_cast<const ulonglong2*>(row + HD);
+        w[0] = w01.x; w[1] = w01.y; w[2] = w23.x; w[3] = w23.y; w[4] = w45.x; w[5] = w45.y;
+        bool ok = true;
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
-          if (c + u * tpi < npieces) {
-            const float* sl = sbase + (c + u * tpi) * step;
-            v[u] = ld_cg4(sl + d);
-            ml[u] = ld_cg2(sl + HD);
-          } else {
-            v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-            ml[u] = make_float2(-INFINITY, 0.f);
-          }
-        }
-        float mb = M;
-#pragma unroll
-        for (int u = 0; u < 16; ++u) mb = fmaxf(mb, ml[u].x);
-        if (mb == -INFINITY) continue;  // only empty pieces so far
-        const float sc = (M == -INFINITY) ? 0.f : fast_exp2(M - mb);
-        O.x *= sc; O.y *= sc; O.z *= sc; O.w *= sc;
-        L *= sc;
-#pragma unroll
-        for (int u = 0; u < 16; ++u) {
-          const float w = (ml[u].x == -INFINITY) ? 0.f : fast_exp2(ml[u].x - mb);
-          O.x += w * v[u].x; O.y += w * v[u].y; O.z += w * v[u].z; O.w += w * v[u].w;
-          L += w * ml[u].y;
-        }
-        M = mb;
+        for (int e = 0; e < 6; ++e) ok = ok && fresh(w[e], ep);
+        if (!ok) poll_piece(src0 + ((int64_t)(p0 + pi) * G + h) * kSH, d, ep, w);
+        fold(O, M, L, w);
       }
-      for (int off = 1; off < tpi; off <<= 1) {
-        const float Mo = __shfl_xor_sync(0xffffffffu, M, off);
-        const float Lo = __shfl_xor_sync(0xffffffffu, L, off);
-        float4 Oo;
-        Oo.x = __shfl_xor_sync(0xffffffffu, O.x, off);
-        Oo.y = __shfl_xor_sync(0xffffffffu, O.y, off);
-        Oo.z = __shfl_xor_sync(0xffffffffu, O.z, off);
-        Oo.w = __shfl_xor_sync(0xffffffffu, O.w, off);
-        const float Mn = fmaxf(M, Mo);
-        const float sa = (M == -INFINITY) ? 0.f : fast_exp2(M - Mn);
-        const float sb = (Mo == -INFINITY) ? 0.f : fast_exp2(Mo - Mn);
-        O.x = O.x * sa + Oo.x * sb; O.y = O.y * sa + Oo.y * sb;
-        O.z = O.z * sa + Oo.z * sb; O.w = O.w * sa + Oo.w * sb;
-        L = L * sa + Lo * sb;
-        M = Mn;
-      }
+    };
+    auto finish_item = [&](int idx, float4& O, float& M, float& L) {
+      const bool active = idx < items * tpi;
+      const int it = active ? idx / tpi : 0, j = idx % tpi;
+      const int h = it / kD4, d = (it - h * kD4) * 4;
+      join(O, M, L, tpi);
       if (active && j == 0) write_final4<HD, XCH>(a, b, g * G + h, d, O, M, L, (uint32_t)flags[2]);
+    };
+    if constexpr (LOADER == 1) {
+      // register-lean (two CTAs an SM): one item pass at a time; the chunks
+      // are copied again for every pass unless all pieces fit in one
+      const bool one_chunk = cap >= npieces;
+      if (one_chunk) copy_chunk(0, npieces);
+      for (int base = 0; base < items * tpi; base += kNCT) {  // warp-uniform trip count
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+        float M = -INFINITY, L = 0.f;
+        for (int p0 = 0; p0 < npieces; p0 += cap) {
+          const int n = imin(cap, npieces - p0);
+          if (!one_chunk) copy_chunk(p0, n);
+          fold_chunk(base + tid, p0, n, O, M, L);
+          if (!one_chunk) consumer_sync(kNCT);  // the chunk is read before the next one lands
+        }
+        finish_item(base + tid, O, M, L);
+      }
+      if (one_chunk) consumer_sync(kNCT);
+    } else {
+      float4 O[kIPT];
+      float M[kIPT], L[kIPT];
+#pragma unroll
+      for (int ip = 0; ip < kIPT; ++ip) {
+        O[ip] = make_float4(0.f, 0.f, 0.f, 0.f);
+        M[ip] = -INFINITY;
+        L[ip] = 0.f;
+      }
+      for (int p0 = 0; p0 < npieces; p0 += cap) {
+        const int n = imin(cap, npieces - p0);
+        copy_chunk(p0, n);
+#pragma unroll
+        for (int ip = 0; ip < kIPT; ++ip) fold_chunk(tid + ip * kNCT, p0, n, O[ip], M[ip], L[ip]);
+        consumer_sync(kNCT);  // the chunk is read before the next one lands
+      }
+#pragma unroll
+      for (int ip = 0; ip < kIPT; ++ip) {
+        if (ip * kNCT >= items * tpi) break;  // warp-uniform: no thread of this pass is active
+        finish_item(tid + ip * kNCT, O[ip], M[ip], L[ip]);
+      }
     }
   };
 
-  auto finish_piece = [&](int b, int g) {
+  // ring_free: no tiles of a later piece of this CTA are in flight or staged.
+  auto finish_piece = [&](int b, int g, bool ring_free, bool first) {
     cons.to_merge(a, merge_w, lane);
+    if (first && tid == 0) mbar_wait(ep_bar, 0, flags, a.status);  // flags[4]: the call epoch
     consumer_sync(kNCT);
     const int s = b * n_kv + g;
     int32_t c0;
     const int32_t npieces = deal.pieces(seq_start, nunits, b, g, &c0);
+    const uint32_t ep = (uint32_t)flags[4];
     // one thread per (head, 4 columns): the warps' (m, l) pairs, then their
     // o chunks, as float2 / float4 shared loads
-    constexpr int kD4 = HD / 4;
     for (int idx = tid; idx < G * kD4; idx += kNCT) {
       const int h = idx / kD4, d = (idx - h * kD4) * 4;
       float2 ml[NW];
@@ -1394,49 +1599,60 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
       if (npieces == 1) {
         write_final4<HD, XCH>(a, b, g * G + h, d, O, M, L, (uint32_t)flags[2]);
       } else {
-        float* slot = a.ws_part + ((int64_t)(blockIdx.x + s) * G + h) * kSH;
-        *reinterpret_cast<float4*>(slot + d) = O;
-        if (d == 0) *reinterpret_cast<float2*>(slot + HD) = make_float2(M, L);
+        uint64_t* slot = a.ws_part + ((int64_t)(blockIdx.x + s) * G + h) * kSH;
+        st_relaxed_gpu_u64x2(slot + d, tag(O.x, ep), tag(O.y, ep));
+        st_relaxed_gpu_u64x2(slot + d + 2, tag(O.z, ep), tag(O.w, ep));
+        if (d == 0) st_relaxed_gpu_u64x2(slot + HD, tag(M, ep), tag(L, ep));
       }
     }
     bool merged_here = npieces == 1;  // this CTA holds the segment's final records
     if (npieces > 1) {
       consumer_sync(kNCT);
       if (tid == 0) {
-        const int old = atomic_add_acq_rel_gpu(&a.ws_counter[s], 1);
+        const int old = atomic_add_relaxed_gpu(&a.ws_counter[s], 1);
         flags[1] = (old == npieces - 1) ? 1 : 0;
       }
       consumer_sync(kNCT);
       merged_here = flags[1] != 0;
+      if (tid == 0) stamp(kTrCounted);
       if (merged_here) {
-        combine_pieces(b, g, s, c0, npieces);
-        if (tid == 0) a.ws_counter[s] = 0;
+        if (ring_free) gather(b, g, s, c0, npieces, ep, smem, a.stages * a.stage_bytes);
+        else gather(b, g, s, c0, npieces, ep, reinterpret_cast<char*>(merge), kMergeBytes);
+        if (tid == 0) st_relaxed_gpu_s32(&a.ws_counter[s], 0);
       }
+    } else if (tid == 0) {
+      stamp(kTrCounted);
     }
     consumer_sync(kNCT);
+    if (merged_here && tid == 0) stamp(kTrMerged);
     if constexpr (XCH) {
       if (merged_here) publish_merge(g);
     }
+    if (merged_here && tid == 0) stamp(kTrPublished);
+    return merged_here;
   };
 
   // Piece by piece, tile by tile: the inner loop carries only the ring
   // position and the row cursor, so the consumer keeps its registers.
-  TileWalk wk;
-  wk.init(seq_start, nunits, B, my_lo, my_lo + my_count);
-  Piece pc;
   int st = 0;
   uint32_t phase = 0;
-  while (wk.next_piece(nunits, B, n_kv, pc)) {
+  auto run_piece = [&](const Piece& pc, int row0, int row_step, bool ring_free,
+                       bool first_piece) {
     // kv head pc.g's exchange epoch (read by every CTA holding a piece of it,
     // advanced only by its publisher), loaded alongside q
     epoch_read(pc.g);
     load_q(pc.b, pc.g);
+    if (first_piece && tid == 0) stamp(kTrQ);
     cons.begin(a, qs, lane);
     const int np = npos[pc.b];
-    int row0 = pc.u0 * unit_rows;
-    for (int k = 0; k < pc.n; ++k, row0 += unit_rows) {
+    const int row_end = row0 + pc.n * row_step;
+    for (; row0 < row_end; row0 += row_step) {
       const int rows = imin(unit_rows, np - row0);
       mbar_wait(&full[st], phase, flags, a.status);
+      if (a.trace && tid == 0 && flags[6] == 0) {
+        stamp(kTrFirstTile);
+        flags[6] = 1;
+      }
       cons.consume(a, smem + (size_t)st * a.stage_bytes, rows, pbuf_w, qs, warp, lane);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
@@ -1445,7 +1661,33 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
         phase ^= 1u;
       }
     }
-    finish_piece(pc.b, pc.g);
+    if (tid == 0) stamp(kTrLastTile);
+    return finish_piece(pc.b, pc.g, ring_free, first_piece);
+  };
+  bool merger = false;
+  if (LOADER == 0 || deal.mode == 1) {  // one piece: kv head g's tiles j, j + S, ...
+    Piece pc;
+    pc.b = 0;
+    pc.g = ct.g;
+    pc.u0 = 0;
+    pc.n = ct.count;
+    merger = run_piece(pc, ct.j * unit_rows, ct.S * unit_rows, true, true);
+  } else if constexpr (LOADER == 1) {  // contiguous deal: piece by piece
+    TileWalk wk = ct.wk;
+    Piece pc;
+    bool first = true;
+    while (wk.next_piece(nunits, B, n_kv, pc)) {
+      merger = run_piece(pc, pc.u0 * unit_rows, unit_rows, wk.p >= wk.end, first) || merger;
+      first = false;
+    }
+  }
+  if (a.trace && tid == 0) {
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    a.trace[(size_t)blockIdx.x * kTraceWords + kTrInfo] =
+        (uint64_t)(uint32_t)my_tiles | ((uint64_t)(flags[5] & 0xff) << 16) |
+        ((uint64_t)(merger ? 1 : 0) << 24) | ((uint64_t)smid << 32);
+    stamp(kTrExit);
   }
 }
 

@@ -156,13 +156,15 @@ GLA_HD int32_t segment_pieces(Split sp, const int32_t* seq_start, const int32_t*
 // How the W units of a call are dealt to P CTAs.
 //  contiguous (mode 0): Split(W, P) over the (b, g, u) order; a CTA range may
 //    straddle segments and then holds several pieces.
-//  per segment (mode 1; one sequence, n_kv <= P): kv head g gets the CTAs of
-//    group g of Split(P, n_kv), which split its nu units evenly, so no CTA
-//    holds more than one piece -- a piece boundary inside a CTA's range
-//    stalls its consumers for a partial write and counter round trip, and a
-//    late CTA becomes its segment's merger.  The largest CTA share is the
-//    same as the contiguous deal's when n_kv divides P, within one unit
-//    otherwise.
+//  round robin per segment (mode 1; one sequence, n_kv <= P): kv head g gets
+//    the S_g CTAs of group g of Split(P, n_kv); CTA j of the group takes the
+//    units j, j + S_g, j + 2 S_g, ... of segment g.  No CTA holds more than
+//    one piece (a piece boundary inside a CTA's range stalls its consumers
+//    for a partial write and counter round trip, and a late CTA becomes its
+//    segment's merger), the shares differ by at most one unit, and which
+//    units a CTA owns does not depend on the segment's length: the first
+//    units of a CTA can be fetched before the length (a position the
+//    preceding kernel may still be writing) is known.
 // Either way the pieces of a segment are consecutive CTAs, and piece
 // (CTA c, segment s) owns partial slot c + s.
 struct Deal {
@@ -170,17 +172,17 @@ struct Deal {
   Split sp;    // mode 0: Split(W, P); mode 1: Split(P, n_kv)
   int32_t nu;  // mode 1: units per segment
 
+  // mode 0: the unit range [lo, lo + cnt) of CTA c in the (b, g, u) order.
   GLA_HD void range(int32_t c, int32_t* lo, int32_t* cnt) const {
-    if (mode == 0) {
-      *lo = split_lo(sp, c);
-      *cnt = split_count(sp, c);
-      return;
-    }
-    const int32_t g = split_owner(sp, c);
-    const Split su = make_split(nu, split_count(sp, g));
-    const int32_t j = c - split_lo(sp, g);
-    *lo = g * nu + split_lo(su, j);
-    *cnt = split_count(su, j);
+    *lo = split_lo(sp, c);
+    *cnt = split_count(sp, c);
+  }
+
+  // mode 1: CTA c's kv head g, its index j in the group and the group size.
+  GLA_HD void group_of(int32_t c, int32_t* g, int32_t* j, int32_t* S) const {
+    *g = split_owner(sp, c);
+    *j = c - split_lo(sp, *g);
+    *S = split_count(sp, *g);
   }
 
   GLA_HD int32_t pieces(const int32_t* seq_start, const int32_t* nunits, int32_t b, int32_t g,
@@ -191,10 +193,17 @@ struct Deal {
   }
 };
 
-// W = total units, P = CTAs, nu0 = units of sequence 0.
+// mode 1: units of a segment of nu units that CTA j of a group of S owns.
+GLA_HD int32_t rr_count(int32_t nu, int32_t j, int32_t S) {
+  return j < nu ? (nu - 1 - j) / S + 1 : 0;
+}
+
+// W = total units, P = CTAs, nu0 = units of sequence 0.  The mode does not
+// depend on the lengths, so a kernel picks the same mode before and after it
+// knows them.
 GLA_HD Deal make_deal(int32_t W, int32_t P, int32_t n_seq, int32_t n_kv, int32_t nu0) {
   Deal d;
-  if (n_seq == 1 && n_kv <= P && nu0 > 0) {
+  if (n_seq == 1 && n_kv <= P) {
     d.mode = 1;
     d.sp = make_split(P, n_kv);
     d.nu = nu0;
@@ -204,6 +213,48 @@ GLA_HD Deal make_deal(int32_t W, int32_t P, int32_t n_seq, int32_t n_kv, int32_t
     d.nu = 0;
   }
   return d;
+}
+
+// The tiles of one CTA in walk (ring) order: mode 1 round robin over one
+// kv head's units (j, j + S, j + 2S, ..., one unit a tile), mode 0 the
+// contiguous unit range walked by TileWalk.
+struct CtaTiles {
+  int32_t mode, g, j, S, k, count;
+  TileWalk wk;
+
+  GLA_HD bool next(const int32_t* nunits, int32_t n_seq, int32_t n_kv, int32_t tile_units,
+                   int32_t unit_rows, Tile& t) {
+    if (mode == 1) {
+      if (k >= count) return false;
+      t.b = 0;
+      t.g = g;
+      t.row0 = (j + k * S) * unit_rows;
+      t.units = 1;
+      ++k;
+      return true;
+    }
+    return wk.next(nunits, n_seq, n_kv, tile_units, unit_rows, t);
+  }
+};
+
+// CTA c's tiles under `deal` (seq_start / nunits as for TileWalk).
+GLA_HD CtaTiles cta_tiles_of(const Deal& deal, int32_t c, const int32_t* seq_start,
+                             const int32_t* nunits, int32_t n_seq) {
+  CtaTiles ct;
+  ct.mode = deal.mode;
+  ct.k = 0;
+  ct.g = ct.j = ct.count = 0;
+  ct.S = 1;
+  if (deal.mode == 1) {
+    deal.group_of(c, &ct.g, &ct.j, &ct.S);
+    ct.count = rr_count(nunits[0], ct.j, ct.S);
+  } else {
+    int32_t lo, cnt;
+    deal.range(c, &lo, &cnt);
+    ct.wk.init(seq_start, nunits, n_seq, lo, lo + cnt);
+    ct.count = cnt;
+  }
+  return ct;
 }
 
 #ifdef __CUDACC__
@@ -350,13 +401,50 @@ __device__ __forceinline__ float4 ld_cg4(const float* p) {
   return __ldcg(reinterpret_cast<const float4*>(p));
 }
 
-// Release/acquire add at GPU scope (one thread, after a CTA barrier: the
-// release covers every write the CTA made before the barrier).
-__device__ __forceinline__ int atomic_add_acq_rel_gpu(int32_t* p, int v) {
+// Relaxed add at GPU scope: the piece counter of a segment.  No ordering is
+// needed because every piece word carries the call's epoch (tagged words).
+__device__ __forceinline__ int atomic_add_relaxed_gpu(int32_t* p, int v) {
   int old;
-  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+  asm volatile("atom.relaxed.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
                : "memory");
   return old;
+}
+
+// GPU-scope relaxed accesses of tagged 64-bit words (value bits | epoch << 32);
+// an aligned 64-bit access is single-copy atomic, so a word that carries the
+// expected epoch carries that call's value.
+__device__ __forceinline__ void st_relaxed_gpu_u64x2(uint64_t* p, uint64_t a, uint64_t b) {
+  asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b)
+               : "memory");
+}
+__device__ __forceinline__ void ld_relaxed_gpu_u64x2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p)
+               : "memory");
+}
+__device__ __forceinline__ int32_t ld_relaxed_gpu_s32(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_gpu_s32(int32_t* p, int32_t v) {
+  asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bulk (non-tensor) copy global -> shared without a cache hint (piece words
+// of the split-KV merge, which stay in L2).
+__device__ __forceinline__ void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes,
+                                               uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Orders this thread's generic-proxy accesses before its later async-proxy
+// (bulk copy) accesses of global memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 // System-scope 64-bit accesses for the peer exchange (another GPU's kernel

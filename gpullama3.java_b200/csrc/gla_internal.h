@@ -48,13 +48,26 @@ struct DecodeRequest {
 
 // Launch geometry chosen for a request.
 struct DecodePlan {
+  int32_t loader;              // 0: tensor-map loader (round-robin deal), 1: cp.async loader
   int32_t tile;
   int32_t stages;
   int32_t grid;
   int32_t threads;
   size_t smem;
-  size_t part_floats;          // workspace floats for piece slots
-  size_t counters;             // workspace counters
+  size_t part_words;           // workspace 64-bit words for piece slots (zeroed when allocated)
+  size_t counters;             // workspace counters (zero between calls)
+};
+
+// Words of the per-CTA phase trace of a decode launch (DecodeWorkspace::trace).
+constexpr int kTraceWordsPerCta = 16;
+
+// Device memory a decode launch uses besides its inputs and outputs.
+struct DecodeWorkspace {
+  uint64_t* part = nullptr;        // plan.part_words tagged piece words, zeroed at allocation
+  int32_t* counter = nullptr;      // plan.counters piece counters, zero between calls
+  unsigned long long* epoch = nullptr;  // one word: call epoch << 32 | tickets of this call
+  int32_t* status = nullptr;       // device status word
+  uint64_t* trace = nullptr;       // optional [grid][16] phase stamps
 };
 
 // Device properties a plan depends on.
@@ -69,8 +82,8 @@ int plan_decode(const DecodeRequest& req, const DeviceInfo& dev, DecodePlan* pla
                 std::string* err);
 
 // Launches the decode kernel with a plan from plan_decode.
-int launch_decode(const DecodeRequest& req, const DecodePlan& plan, float* ws_part,
-                  int32_t* ws_counter, int32_t* status, cudaStream_t stream, std::string* err);
+int launch_decode(const DecodeRequest& req, const DecodePlan& plan, const DecodeWorkspace& ws,
+                  cudaStream_t stream, std::string* err);
 
 // Log-sum-exp merge of records [n_parts][n_heads][head_dim+2] into xb.
 int launch_lse_combine(const float* parts, int32_t n_parts, int32_t n_heads, int32_t head_dim,
@@ -115,5 +128,10 @@ int launch_ingest(bool f16_cache, const float* q, const float* k, const float* v
                   int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, float theta,
                   int32_t rope_style, int32_t* status, const DeviceInfo& dev,
                   cudaStream_t stream, std::string* err);
+
+// Test hook (debug.cu): a PDL kernel that releases its dependents at once,
+// spins delay_us (at most 1000) and then adds delta to *position_holder.
+int launch_advance_position(int32_t* position_holder, int32_t delta, int32_t delay_us,
+                            cudaStream_t stream, std::string* err);
 
 }  // namespace gla

@@ -28,6 +28,18 @@ class PeerExchange {
   // be enabled (active() says which), an error code only when the
   // collective itself failed.
   int setup(Comm& comm, cudaStream_t stream, std::string* err);
+  // Test hook: one process plays rank 0 of a `world`-rank exchange whose
+  // other ranks' buffers are local allocations nobody else writes, so the
+  // kernel's wait for their records runs out (bounded) and latches
+  // GLA_ERR_TIMEOUT.
+  int setup_loopback(int world, std::string* err);
+  bool loopback() const { return loopback_; }
+  // Zeroes this rank's buffer (records and epochs), stream ordered.  Only
+  // between two barriers of every rank: no peer may be writing into it.
+  int reset(cudaStream_t stream, std::string* err);
+  // Closes the peers' mappings and frees this rank's buffer.  Only after a
+  // barrier of every rank (no peer still stores into it), or after the
+  // communicator was aborted.
   void teardown();
   bool active() const { return active_; }
 
@@ -41,6 +53,8 @@ class PeerExchange {
   void* local_ = nullptr;
   uint64_t* d_bases_ = nullptr;
   std::vector<void*> opened_;  // peers' buffers mapped here (to close)
+  std::vector<void*> owned_;   // loopback: the stand-in peers' buffers (to free)
+  bool loopback_ = false;
 };
 
 }  // namespace gla

@@ -18,10 +18,12 @@
 //
 // Sharing: every call on a device uses the same array and it keeps the last
 // call's contents.  Each call clears the status word and the counters it uses
-// (one cudaMemsetAsync on the caller's stream) before its kernel; the partial
-// records need no clearing (each is written before it is read).  Calls whose
-// kernels overlap on the GPU (different streams without ordering, or threads
-// racing on one device) race on the array and give wrong results.
+// (one cudaMemsetAsync on the caller's stream) before its kernel.  The
+// partial records need no clearing: each word carries the epoch of the call
+// that wrote it, and the epoch word (never cleared; zero when the library is
+// loaded) gives every call a larger one.  Calls whose kernels overlap on the
+// GPU (different streams without ordering, or threads racing on one device)
+// race on the array and give wrong results.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -34,11 +36,15 @@
 
 namespace {
 
-// Layout of the scratch array: [0, 256) status word, [256, 256 + 4 * kMaxCounters)
-// arrival counters, [kHeaderBytes, kHeaderBytes + kSlotBytes) partial records.
+// Layout of the scratch array: [0, 4) status word, [16, 16 + 4 * kMaxCounters)
+// arrival counters, [kEpochOffset, +8) the call-epoch word,
+// [kHeaderBytes, kHeaderBytes + kSlotBytes) partial records.
 constexpr size_t kMaxCounters = 1024;                // kv heads of one call
-constexpr size_t kHeaderBytes = 8192;                // status + counters, padded
+constexpr size_t kCounterOffset = 16;
+constexpr size_t kEpochOffset = 8184;
+constexpr size_t kHeaderBytes = 8192;                // status, counters, epoch
 constexpr size_t kSlotBytes = size_t(1) << 20;       // 1 MiB of partial records
+static_assert(kCounterOffset + 4 * kMaxCounters <= kEpochOffset, "header layout");
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kHeaderBytes + kSlotBytes];
@@ -118,23 +124,27 @@ extern "C" int32_t gla_decode_f32kv_noalloc(const float* q, const float* k, cons
   req.scale = scale;
   req.out = xb;
   req.record_mode = 0;
+  req.early_kv = 1;  // n_pos comes from the host: the same kernel path as gla_decode_f32kv
 
   std::string err;
   gla::DecodePlan plan;
   rc = gla::plan_decode(req, d->info, &plan, &err);
   if (rc != GLA_OK) return rc;
   // the scratch has a fixed size: refuse calls that need more
-  if (plan.counters > kMaxCounters || plan.part_floats * sizeof(float) > kSlotBytes)
+  if (plan.counters > kMaxCounters || plan.part_words * sizeof(uint64_t) > kSlotBytes)
     return GLA_ERR_NOT_SUPPORTED;
 
   cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
-  int32_t* status = reinterpret_cast<int32_t*>(d->base);
-  int32_t* counters = reinterpret_cast<int32_t*>(d->base + 256);
-  float* parts = reinterpret_cast<float*>(d->base + kHeaderBytes);
-  // status word and this call's counters start at zero
-  if (cudaMemsetAsync(d->base, 0, 256 + plan.counters * sizeof(int32_t), stream) != cudaSuccess) {
+  gla::DecodeWorkspace ws;
+  ws.status = reinterpret_cast<int32_t*>(d->base);
+  ws.counter = reinterpret_cast<int32_t*>(d->base + kCounterOffset);
+  ws.epoch = reinterpret_cast<unsigned long long*>(d->base + kEpochOffset);
+  ws.part = reinterpret_cast<uint64_t*>(d->base + kHeaderBytes);
+  // status word and this call's counters start at zero (the epoch word stays)
+  if (cudaMemsetAsync(d->base, 0, kCounterOffset + plan.counters * sizeof(int32_t), stream) !=
+      cudaSuccess) {
     cudaGetLastError();
     return GLA_ERR_CUDA;
   }
-  return gla::launch_decode(req, plan, parts, counters, status, stream, &err);
+  return gla::launch_decode(req, plan, ws, stream, &err);
 }

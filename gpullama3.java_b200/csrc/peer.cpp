@@ -31,12 +31,12 @@ int agree(Comm& comm, bool mine, cudaStream_t stream, bool* all, std::string* er
   }
   if (rc == GLA_OK) rc = comm.all_gather(d, d + 1, 1, stream, err);
   if (rc == GLA_OK &&
-      (cudaMemcpyAsync(h.data(), d + 1, sizeof(float) * n, cudaMemcpyDeviceToHost, stream) !=
-           cudaSuccess ||
-       cudaStreamSynchronize(stream) != cudaSuccess)) {
+      cudaMemcpyAsync(h.data(), d + 1, sizeof(float) * n, cudaMemcpyDeviceToHost, stream) !=
+          cudaSuccess) {
     *err = "peer exchange: copy failed";
     rc = GLA_ERR_CUDA;
   }
+  if (rc == GLA_OK) rc = comm.wait(stream, err);
   cudaFree(d);
   bool ok = true;
   for (float x : h) ok = ok && x == 1.f;
@@ -78,12 +78,12 @@ int PeerExchange::setup(Comm& comm, cudaStream_t stream, std::string* err) {
   }
   if (rc == GLA_OK) rc = comm.all_gather(d, d + kF, kF, stream, err);
   if (rc == GLA_OK &&
-      (cudaMemcpyAsync(recv.data(), d + kF, sizeof(float) * kF * n, cudaMemcpyDeviceToHost,
-                       stream) != cudaSuccess ||
-       cudaStreamSynchronize(stream) != cudaSuccess)) {
+      cudaMemcpyAsync(recv.data(), d + kF, sizeof(float) * kF * n, cudaMemcpyDeviceToHost,
+                      stream) != cudaSuccess) {
     *err = "peer exchange: copy failed";
     rc = GLA_ERR_CUDA;
   }
+  if (rc == GLA_OK) rc = comm.wait(stream, err);
   cudaFree(d);
   if (rc != GLA_OK) {
     teardown();
@@ -129,9 +129,57 @@ int PeerExchange::setup(Comm& comm, cudaStream_t stream, std::string* err) {
   return GLA_OK;
 }
 
+int PeerExchange::setup_loopback(int n, std::string* err) {
+  teardown();
+  if (n < 2 || n > kXchMaxWorld) {
+    *err = "loopback world must be in [2, 8]";
+    return GLA_ERR_INVALID_ARG;
+  }
+  std::vector<uint64_t> bases(n, 0);
+  for (int r = 0; r < n; ++r) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, xch_bytes()) != cudaSuccess || cudaMemset(p, 0, xch_bytes()) != cudaSuccess) {
+      cudaGetLastError();
+      if (p) cudaFree(p);
+      teardown();
+      *err = "loopback exchange allocation failed";
+      return GLA_ERR_OUT_OF_MEMORY;
+    }
+    if (r == 0) local_ = p;
+    else owned_.push_back(p);
+    bases[r] = reinterpret_cast<uint64_t>(p);
+  }
+  if (cudaMalloc(&d_bases_, sizeof(uint64_t) * n) != cudaSuccess ||
+      cudaMemcpy(d_bases_, bases.data(), sizeof(uint64_t) * n, cudaMemcpyHostToDevice) !=
+          cudaSuccess) {
+    cudaGetLastError();
+    teardown();
+    *err = "loopback exchange allocation failed";
+    return GLA_ERR_OUT_OF_MEMORY;
+  }
+  world = n;
+  rank = 0;
+  active_ = true;
+  loopback_ = true;
+  return GLA_OK;
+}
+
+int PeerExchange::reset(cudaStream_t stream, std::string* err) {
+  if (!local_) return GLA_OK;
+  if (cudaMemsetAsync(local_, 0, xch_bytes(), stream) != cudaSuccess) {
+    cudaGetLastError();
+    *err = "peer exchange: reset failed";
+    return GLA_ERR_CUDA;
+  }
+  return GLA_OK;
+}
+
 void PeerExchange::teardown() {
   for (void* p : opened_) cudaIpcCloseMemHandle(p);
   opened_.clear();
+  for (void* p : owned_) cudaFree(p);
+  owned_.clear();
+  loopback_ = false;
   if (d_bases_) cudaFree(d_bases_);
   d_bases_ = nullptr;
   if (local_) cudaFree(local_);

@@ -15,7 +15,7 @@ import math
 import os
 
 __all__ = ["GlaError", "Context", "lib", "LIB_PATH", "DTYPE_F32", "DTYPE_F16",
-           "ROPE_INTERLEAVED", "ROPE_NEOX", "EXPORTED_SYMBOLS", "debug_partition"]
+           "ROPE_INTERLEAVED", "ROPE_NEOX", "EXPORTED_SYMBOLS", "debug_partition", "device_view"]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libgpullama_attn.so")
 
@@ -27,6 +27,8 @@ ROPE_INTERLEAVED = 0
 ROPE_NEOX = 1
 OPT_EARLY_KV_PREFETCH = 1  # values: 0 off, 1 host n_pos, 2 (default) also device positions
 OPT_SHARD_EXCHANGE = 2     # 1 (default): peer exchange when available, 0: NCCL all-gather
+OPT_COMM_TIMEOUT_MS = 3    # host deadline of every step that waits for other ranks
+OPT_TRACE = 4              # 1: decode calls record per-CTA phase stamps (debug_trace)
 
 STATUS_NAMES = {
     0: "GLA_OK", -1: "GLA_ERR_INVALID_ARG", -2: "GLA_ERR_CUDA", -3: "GLA_ERR_NOT_SUPPORTED",
@@ -74,9 +76,14 @@ _SIGS = {
     "gla_decode_sharded_f32kv": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F]),
     "gla_prefill_causal_f16": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _F]),
     "gla_rope_append_f32": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P, _F, _I32]),
+    "gla_debug_trace": (_I64, [_P, _P, _I64]),
+    "gla_debug_advance_position": (_I32, [_P, _P, _I32, _I32]),
+    "gla_debug_xch_loopback": (_I32, [_P, _I32]),
     "gla_debug_partition": (_I64, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P,
                                    _P, _P, _I64]),
     "gla_comm_peer_exchange": (_I32, [_P]),
+    "gla_comm_wait": (_I32, [_P]),
+    "gla_comm_resync": (_I32, [_P]),
     "gla_rope_append_attention_f32": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32,
                                              _P, _I32, _I32, _F, _I32]),
     "gla_decode_f32kv_noalloc": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I64, _I32, _F, _P]),
@@ -131,6 +138,23 @@ def _ptr(x) -> int | None:
     if dp is not None:
         return int(dp())
     raise TypeError(f"expected a device tensor or an address, got {type(x)!r}")
+
+
+def device_view(address: int, shape, dtype):
+    """A torch CUDA tensor viewing `address` (device memory the library
+    allocated, e.g. a KV cache from gla_kv_cache_alloc) without copying; it
+    must not outlive the allocation."""
+    import torch
+
+    typestr = {torch.float32: "<f4", torch.float16: "<f2", torch.int8: "|i1",
+               torch.int16: "<i2", torch.int32: "<i4", torch.uint8: "|u1"}[dtype]
+
+    class _View:
+        __cuda_array_interface__ = {"shape": tuple(int(x) for x in shape), "typestr": typestr,
+                                    "data": (int(address), False), "version": 3,
+                                    "strides": None}
+
+    return torch.as_tensor(_View(), device="cuda")
 
 
 def debug_partition(n_pos, n_kv_heads, tile, n_ctas, unit_rows=64):
@@ -209,6 +233,27 @@ class Context:
         self._check(self._L.gla_device_status(self._h, ctypes.byref(st)), "gla_device_status")
         return int(st.value)
 
+    def debug_trace(self):
+        """Phase stamps of the last decode launch: uint64 array [CTA][16]
+        (GLA_OPT_TRACE must be on)."""
+        import numpy as np
+
+        cap = 2 * self.num_sms() * 16
+        out = np.zeros(cap, dtype=np.uint64)
+        n = self._L.gla_debug_trace(self._h, out.ctypes.data, cap)
+        if n < 0:
+            self._check(int(n), "gla_debug_trace")
+        return out[:n].reshape(-1, 16)
+
+    def debug_advance_position(self, position_holder, delta, delay_us=20):
+        """Test hook: a PDL kernel that adds delta to the device position."""
+        self._check(self._L.gla_debug_advance_position(self._h, _ptr(position_holder), delta,
+                                                       delay_us), "gla_debug_advance_position")
+
+    def debug_xch_loopback(self, world):
+        """Test hook: a one-process peer exchange whose other ranks never write."""
+        self._check(self._L.gla_debug_xch_loopback(self._h, world), "gla_debug_xch_loopback")
+
     def reserve(self, max_batch, max_kv_heads, max_heads, max_head_dim):
         self._check(self._L.gla_reserve(self._h, max_batch, max_kv_heads, max_heads, max_head_dim),
                     "gla_reserve")
@@ -284,6 +329,14 @@ class Context:
     def comm_init(self, nranks: int, rank: int, unique_id: bytes):
         buf = ctypes.create_string_buffer(unique_id, len(unique_id))
         self._check(self._L.gla_comm_init(self._h, nranks, rank, buf), "gla_comm_init")
+
+    def comm_wait(self):
+        """gla_comm_wait: bounded stream drain (aborts a stuck communicator)."""
+        self._check(self._L.gla_comm_wait(self._h), "gla_comm_wait")
+
+    def comm_resync(self):
+        """gla_comm_resync: collective reset of the peer exchange epochs."""
+        self._check(self._L.gla_comm_resync(self._h), "gla_comm_resync")
 
     @property
     def peer_exchange(self) -> bool:

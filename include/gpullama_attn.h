@@ -68,7 +68,12 @@ const char* gla_status_string(int32_t status);
  * attention task. */
 int32_t gla_create(int32_t device, void* cuda_stream, gla_ctx** out);
 
-/* Frees the context, its workspace and its communicator (if any). */
+/* Frees the context, its workspace and its communicator (if any).
+ * Collective for a context with a communicator (gla_comm_init): every rank
+ * calls it; the ranks meet at a bounded barrier before the peer exchange
+ * buffers that other ranks store into are unmapped and freed.  Returns
+ * GLA_ERR_TIMEOUT (after freeing everything) if a rank did not arrive within
+ * the communicator timeout. */
 int32_t gla_destroy(gla_ctx* ctx);
 
 /* Re-targets the context to another stream of the same device. */
@@ -114,6 +119,22 @@ int32_t gla_num_sms(const gla_ctx* ctx);
  * value if a kernel that runs right before a decode call and releases its
  * dependents early writes older cache rows (use 0) or the positions (use 1).
  * (Early reads apply to the tensor-map loader: single-sequence calls.) */
+#define GLA_OPT_COMM_TIMEOUT_MS 3
+/* GLA_OPT_COMM_TIMEOUT_MS (default 60000): host deadline of every step that
+ * waits for other ranks - joining the communicator, enqueueing a collective,
+ * gla_comm_wait / gla_device_status on a context with a communicator,
+ * gla_comm_resync and the barrier of gla_destroy.  Past it the NCCL
+ * communicator is aborted (ncclCommAbort ends its kernels), the call returns
+ * GLA_ERR_TIMEOUT and sharded decode needs gla_comm_init again.  No
+ * reference counterpart (the reference is single-device). */
+#define GLA_OPT_TRACE 4
+/* GLA_OPT_TRACE (default 0): 1 = every decode call on the context writes
+ * %globaltimer stamps of its phases (16 words per CTA: entry, dependency
+ * wait, q loaded, first tile, last tile, piece counted, merged, published,
+ * producer first/last copy, info, exit), read back with gla_debug_trace.
+ * Turn it on outside stream capture.  No reference counterpart (the
+ * reference's TornadoVM profiler flags, llama-tornado:93-134, time whole
+ * tasks). */
 #define GLA_OPT_SHARD_EXCHANGE 2
 /* GLA_OPT_SHARD_EXCHANGE (default 1): 1 = sharded decode merges over the
  * peer exchange when gla_comm_init could set it up, 0 = always the NCCL
@@ -335,6 +356,23 @@ int32_t gla_comm_init(gla_ctx* ctx, int32_t nranks, int32_t rank, const void* un
  * the NCCL all-gather.  No reference counterpart (introspection). */
 int32_t gla_comm_peer_exchange(const gla_ctx* ctx);
 
+/* Host watchdog: waits until the context's stream has drained, at most
+ * GLA_OPT_COMM_TIMEOUT_MS.  A collective still waiting for a rank at the
+ * deadline (a rank left, or skipped a call) is ended by aborting the
+ * communicator: returns GLA_ERR_TIMEOUT and the context needs gla_comm_init
+ * again (collectively, with the ranks still present).  Without a
+ * communicator: a plain stream synchronisation.  No reference counterpart. */
+int32_t gla_comm_wait(gla_ctx* ctx);
+
+/* Collective recovery of the peer exchange after a sharded call returned
+ * GLA_ERR_TIMEOUT in the device status (a rank skipped or lost a call, so
+ * the ranks' per-kv-head call epochs differ): every rank drains its stream,
+ * meets at a barrier, zeroes its exchange buffer (records and epochs), the
+ * device status and the piece counters, and meets again.  Later calls
+ * start from matching epochs.  Bounded like gla_comm_wait.  No reference
+ * counterpart. */
+int32_t gla_comm_resync(gla_ctx* ctx);
+
 /* Decode of one sequence whose KV rows are sharded across the communicator's
  * ranks (this rank holds n_pos_local >= 0 rows).  Every rank ends with the
  * full xb.  Peer exchange (gla_comm_peer_exchange() == 1): one kernel
@@ -439,11 +477,34 @@ int32_t gla_rope_append_f32(gla_ctx* ctx, float* q, float* k, const float* v, fl
 /* Introspection used by the host tests (no device work)                     */
 /* ------------------------------------------------------------------------ */
 
+/* Test hook: launches on the context's stream a kernel standing in for a
+ * caller's own position update - it releases its dependents at once
+ * (programmatic dependent launch), spins delay_us (at most 1000), then adds
+ * `delta` to position_holder[0].  A decode call behind it must attend to the
+ * new position.  No reference counterpart. */
+int32_t gla_debug_advance_position(gla_ctx* ctx, int32_t* position_holder, int32_t delta,
+                                   int32_t delay_us);
+
+/* Test hook: makes the context play rank 0 of a `world`-rank peer exchange
+ * (2..8) whose other ranks' buffers are local allocations that nobody
+ * writes, so a sharded call's bounded wait for their records runs out and
+ * latches GLA_ERR_TIMEOUT in the device status.  world = 0 removes it.  Only
+ * on a context without a communicator.  No reference counterpart. */
+int32_t gla_debug_xch_loopback(gla_ctx* ctx, int32_t world);
+
+/* Copies up to `capacity` words of the phase trace of the context's last
+ * decode launch (GLA_OPT_TRACE) to host memory `out`, after synchronising
+ * the stream: [CTA][16] uint64 (%globaltimer ns; word 10 = tiles | early
+ * tiles << 16 | merger << 24 | SM id << 32).  Returns the words copied or a
+ * negative status.  No reference counterpart. */
+int64_t gla_debug_trace(gla_ctx* ctx, uint64_t* out, int64_t capacity);
+
 /* Runs the decode kernels' work partition on the host: `n_seq` sequences with
  * n_pos[] rows, n_kv_heads segments each, dealt to `n_ctas` CTAs in units of
  * `unit_rows` rows and walked in tiles of up to `tile` rows (a multiple of
- * unit_rows).  Writes for every tile, in walk order, its CTA, sequence, kv
- * head, first row, row count, partial-slot index, and the first CTA and
+ * unit_rows; one sequence with n_kv_heads <= n_ctas: round robin, one unit a
+ * tile).  Writes for every tile, in each CTA's walk order, its CTA, sequence,
+ * kv head, first row, row count, partial-slot index, and the first CTA and
  * number of CTAs holding a piece of its segment (the merge's view) into the
  * eight arrays (each of length `capacity`); returns the tile count or a
  * negative status. */

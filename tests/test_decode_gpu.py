@@ -386,3 +386,86 @@ def test_fused_rope_append_attention_equals_separate_calls(gla_ctx, style, hd, n
     with pytest.raises(gla.GlaError):
         gla_ctx.rope_append_attention(q2, k2, v2, kc2, vc2, xb2, nh, hd, kvd, nh // nkv, ph,
                                       layer, ctxlen, theta, 7)
+
+
+def _foreign_pdl_case(gla_ctx, oracle, delta, fused):
+    import gpullama_attn as gla
+
+    torch = _torch()
+    nh, nkv, hd, ctxlen = 24, 8, 128, 2048
+    pos0 = 700
+    q0, k, v = inputs.decode_case(61 + delta, nh, nkv, hd, ctxlen)
+    rng = np.random.Generator(np.random.PCG64(62))
+    knew = rng.standard_normal(nkv * hd, dtype=np.float32)
+    vnew = rng.standard_normal(nkv * hd, dtype=np.float32)
+    kc, vc = dev(k), dev(v)
+    qd, kd, vd = dev(q0), dev(knew), dev(vnew)
+    ph = torch.tensor([pos0], dtype=torch.int32, device="cuda")
+    xb = torch.empty(nh * hd, device="cuda")
+    scratch = torch.empty(nh * hd, device="cuda")
+    assert gla_ctx.device_status() == 0
+    for _ in range(3):  # decodes that release their dependents early, ahead of it
+        gla_ctx.decode(qd, kc, vc, scratch, nh, nkv, hd, pos0 + 1)
+    gla_ctx.debug_advance_position(ph, delta, delay_us=30)
+    if fused:
+        gla_ctx.rope_append_attention(qd, kd, vd, kc, vc, xb, nh, hd, nkv * hd, nh // nkv, ph, 0,
+                                      ctxlen, 500000.0)
+    else:
+        gla_ctx.process_heads_flash_attention(qd, kc, vc, xb, nh, hd, nkv * hd, nh // nkv, ph, 0,
+                                              ctxlen)
+    assert gla_ctx.device_status() == 0
+    assert int(ph.item()) == pos0 + delta
+    pos = pos0 + delta
+    kk, vv = kc.cpu().numpy(), vc.cpu().numpy()
+    if fused:
+        # the reference: RoPE of q and the new key at `pos`, append, attend
+        cr, ci = oracle.rope_freqs(ctxlen, hd, 500000.0)
+        qq, kn = q0.copy(), knew.copy()
+        oracle.rope_interleaved(qq, kn, hd, pos, cr, ci)
+        np.testing.assert_allclose(kk[pos], kn, rtol=0, atol=2e-6)
+        np.testing.assert_array_equal(vv[pos], vnew)
+    else:
+        qq = q0
+    ref = oracle.decode_f32(qq, kk, vv, nh, nkv, hd, pos + 1)
+    assert_close(xb.cpu().numpy(), ref, TOL_F32, f"delta {delta}, fused {fused}")
+
+
+@pytest.mark.parametrize("fused", [False, True], ids=["task", "fused-rope"])
+@pytest.mark.parametrize("delta", [1, 64, 300])
+def test_decode_after_foreign_pdl_position_update(gla_ctx, oracle, delta, fused):
+    import gpullama_attn as gla
+
+    gla_ctx.set_option(gla.OPT_EARLY_KV_PREFETCH, 2)  # the default level
+    _foreign_pdl_case(gla_ctx, oracle, delta, fused)
+
+
+def test_phase_trace_option(gla_ctx):
+    """GLA_OPT_TRACE: every CTA of the last decode launch leaves ordered
+    %globaltimer stamps; the tiles it reports add up to the launch's tiles
+    (C2 layer shape: 8 kv heads x 64 tiles) and exactly one CTA a kv head
+    merges (more than one CTA per kv head hold a piece)."""
+    import gpullama_attn as gla
+
+    torch = _torch()
+    nh, nkv, hd, n = 24, 8, 128, 4096
+    q, k, v = inputs.decode_case(5, nh, nkv, hd, n)
+    qd, kd, vd = dev(q), dev(k), dev(v)
+    xb = torch.empty(nh * hd, device="cuda")
+    gla_ctx.set_option(gla.OPT_TRACE, 1)
+    try:
+        gla_ctx.decode(qd, kd, vd, xb, nh, nkv, hd, n)
+        tr = gla_ctx.debug_trace()
+    finally:
+        gla_ctx.set_option(gla.OPT_TRACE, 0)
+    assert gla_ctx.device_status() == 0
+    ctas = gla_ctx.num_sms()
+    tr = tr[:ctas]
+    info = tr[:, 10]
+    tiles = (info & 0xFFFF).astype(np.int64)
+    merger = (info >> 24) & 0xFF
+    assert int(tiles.sum()) == nkv * (n // 64)
+    assert int(merger.sum()) == nkv
+    work = tiles > 0
+    for col_a, col_b in ((0, 1), (1, 2), (2, 3), (3, 4), (4, 5), (5, 11)):
+        assert np.all(tr[work, col_a] <= tr[work, col_b]), (col_a, col_b)
+    assert np.all(tr[merger == 1, 5] <= tr[merger == 1, 6])

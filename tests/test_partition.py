@@ -13,9 +13,11 @@ def check(n_pos, n_kv, tile, n_ctas, unit=64):
     r = gla.debug_partition(n_pos, n_kv, tile, n_ctas, unit)
     n_pos = [max(0, int(x)) for x in n_pos]
     per_segment = len(n_pos) == 1 and n_kv <= n_ctas and n_pos[0] > 0
-    # every row of every segment is covered exactly once, in order
+    # every row of every segment is covered exactly once (one sequence with
+    # n_kv <= CTAs: CTA j of a kv head's group of S takes tiles j, j+S, ...;
+    # otherwise contiguous ranges walked in order)
     covered = {}
-    for s, g, r0, nr in zip(r["seq"], r["kv_head"], r["row0"], r["rows"]):
+    for c, s, g, r0, nr in zip(r["cta"], r["seq"], r["kv_head"], r["row0"], r["rows"]):
         assert 0 < nr <= tile and r0 % unit == 0
         covered.setdefault((int(s), int(g)), []).append((int(r0), int(nr)))
     for b, n in enumerate(n_pos):
@@ -24,11 +26,29 @@ def check(n_pos, n_kv, tile, n_ctas, unit=64):
             if n == 0:
                 assert not spans
                 continue
+            if not per_segment:  # contiguous deal: the walk order is the row order
+                assert [r0 for r0, _ in spans] == sorted(r0 for r0, _ in spans)
             pos = 0
-            for r0, nr in spans:
+            for r0, nr in sorted(spans):
                 assert r0 == pos
                 pos += nr
             assert pos == n, (b, g, spans)
+    if per_segment:
+        # round robin: a CTA's tiles are S tiles apart, and which tiles a CTA
+        # owns does not depend on the length (a prefix of its infinite list)
+        by_cta = {}
+        for c, g, r0 in zip(r["cta"], r["kv_head"], r["row0"]):
+            by_cta.setdefault(int(c), []).append((int(g), int(r0) // unit))
+        groups = {}
+        for c, lst in by_cta.items():
+            assert len({g for g, _ in lst}) == 1
+            groups.setdefault(lst[0][0], []).append(c)
+        for g, cs in groups.items():
+            cs = sorted(cs)
+            lo, S = cs[0], n_ctas // n_kv + (1 if g < n_ctas % n_kv else 0)
+            for c in cs:
+                j = c - lo
+                assert [t for _, t in by_cta[c]] == list(range(j, j + S * len(by_cta[c]), S))
     if len(r["cta"]) == 0:
         return r
     cta = r["cta"]
