@@ -58,7 +58,7 @@ Layout layout_for(int dtype, int hd, int group, int tile, int stages, int batch,
   Layout L;
   size_t off = (size_t)stages * stage_bytes_for(dtype, hd, tile);
   L.off_bars = (int32_t)align16(off);
-  off = L.off_bars + (size_t)(stages * 3 + 2) * sizeof(uint64_t);  // full, empty, land, merge, epoch
+  off = L.off_bars + (size_t)(stages * 3 + 1) * sizeof(uint64_t);  // full, empty, land, epoch
   L.off_seq = (int32_t)align16(off);
   off = L.off_seq + (size_t)(3 * batch + 1) * sizeof(int32_t);
   L.off_q = (int32_t)align16(off);

@@ -893,8 +893,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bars);
   uint64_t* empty = full + a.stages;
   uint64_t* land = empty + a.stages;  // early copies (issued before the dependency wait)
-  uint64_t* mbar = land + a.stages;   // piece gathers of the merge
-  uint64_t* ep_bar = mbar + 1;        // the call epoch is in flags[4]
+  uint64_t* ep_bar = land + a.stages;  // the call epoch is in flags[4]
   int32_t* seq_start = reinterpret_cast<int32_t*>(smem + a.off_seq);  // [B+1] (units)
   int32_t* nunits = seq_start + (B + 1);                              // [B]
   int32_t* npos = nunits + B;                                         // [B]
@@ -940,7 +939,6 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
       mbar_init(&empty[s], NW);
       mbar_init(&land[s], 1);
     }
-    mbar_init(mbar, 1);
     mbar_init(ep_bar, 1);
     flags[0] = 0;
     flags[1] = 0;
@@ -1136,13 +1134,15 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
       int32_t seg = -1;
       while (n_early < a.stages && ct.next(nus, 1, n_kv, 1, unit_rows, t)) {
         if (lane == 0) {
-          // fused RoPE: warm L2 with the inputs read right after the wait (the
-          // group's q vectors, the new key and value rows of kv head g)
-          if (a.rope && t.g != seg) {
+          // warm L2 with the inputs read right after the wait (the group's
+          // q vectors; fused RoPE: the new key and value rows of kv head g)
+          if (t.g != seg) {
             seg = t.g;
             prefetch_l2_bulk(a.q + (int64_t)t.g * G * HD, (uint32_t)(G * HD * sizeof(float)));
-            prefetch_l2_bulk(a.rope_k + (int64_t)t.g * HD, (uint32_t)(HD * sizeof(float)));
-            prefetch_l2_bulk(a.rope_v + (int64_t)t.g * HD, (uint32_t)(HD * sizeof(float)));
+            if (a.rope) {
+              prefetch_l2_bulk(a.rope_k + (int64_t)t.g * HD, (uint32_t)(HD * sizeof(float)));
+              prefetch_l2_bulk(a.rope_v + (int64_t)t.g * HD, (uint32_t)(HD * sizeof(float)));
+            }
           }
           tma_tile(n_early, t, pol, &land[n_early]);
         }
@@ -1177,6 +1177,18 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
     // has long arrived; the consumers read it behind ep_bar.
     unsigned long long ticket = 0;
     if (lane == 31) ticket = atomicAdd(a.ws_epoch, 1ull);
+    auto settle_ticket = [&]() {
+      if (lane == 31) {
+        const uint32_t call_ep = (uint32_t)(ticket >> 32) + 1u;
+        flags[4] = (int)call_ep;
+        if ((uint32_t)ticket == (uint32_t)P - 1u)
+          atomicExch(a.ws_epoch, (unsigned long long)call_ep << 32);
+        mbar_arrive(ep_bar);
+      }
+    };
+    // contiguous deal: a CTA may finish a piece (and need the epoch) while
+    // this warp still waits for ring slots of its next piece, so settle now
+    if (deal.mode == 0) settle_ticket();
     const uint64_t pol = l2_evict_first_policy();
     CtaTiles ct = cta_tiles();
     Tile t;
@@ -1246,13 +1258,8 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
       }
     }
     if (lane == 0) stamp(kTrProdLast);
-    if (lane == 31) {
-      const uint32_t call_ep = (uint32_t)(ticket >> 32) + 1u;
-      flags[4] = (int)call_ep;
-      if ((uint32_t)ticket == (uint32_t)P - 1u)
-        atomicExch(a.ws_epoch, (unsigned long long)call_ep << 32);
-      mbar_arrive(ep_bar);
-    }
+    // round robin: the one piece ends after its last tile was issued
+    if (deal.mode == 1) settle_ticket();
     return;
   }
 
@@ -1357,7 +1364,6 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
   float* merge_w = merge + warp * kMG * kMH;
   constexpr int kSH = slot_head_floats<HD>();  // words per head in a piece slot
   constexpr int kMergeBytes = NW * kMG * kMH * (int)sizeof(float);  // the warp merge buffer
-  uint32_t gather_phase = 0;  // completed phases of the merge barrier
 
   // The group's q vectors, pre-scaled by scale*log2(e), rows >= G zeroed.
   auto load_q = [&](int b, int g) {
@@ -1471,10 +1477,10 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
   };
 
   // Merger: the segment's slots c0 + s .. c0 + s + npieces - 1 (consecutive)
-  // are bulk-copied into shared memory `dst` (the drained ring, or the warp
-  // merge buffer when the ring still holds this CTA's next piece) in chunks
-  // of whole pieces; every thread folds its items' pieces from there (words
-  // of another call are polled again from global memory).
+  // are copied into shared memory `dst` (the drained ring, or the warp merge
+  // buffer when the ring still holds this CTA's next piece) in chunks of
+  // whole pieces; every thread folds its items' pieces from there (words a
+  // piece's CTA has not stored yet are polled again from global memory).
   auto gather = [&](int b, int g, int s, int c0, int npieces, uint32_t ep, char* dst_bytes,
                     int cap_bytes) {
     int tpi;
@@ -1488,14 +1494,15 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
     // overwrites the ring
     if (tid == 0 && dst_bytes == smem)
       for (int k = my_tiles; k < flags[5]; ++k) mbar_wait(&land[k], 0, flags, a.status);
+    // every consumer thread copies its share of the chunk's 16-byte words
+    // (cp.async: no registers, all copies in flight at once)
     auto copy_chunk = [&](int p0, int n) {
-      if (tid == 0) {
-        fence_proxy_async_global();  // this CTA's own piece stores, before the copy
-        const uint32_t bytes = (uint32_t)(n * piece_words * 8);
-        mbar_arrive_expect_tx(mbar, bytes);
-        bulk_g2s_plain(dst, src0 + (int64_t)p0 * piece_words, bytes, mbar);
-      }
-      mbar_wait(mbar, (uint32_t)(gather_phase++ & 1), flags, a.status);
+      const int n16 = n * piece_words / 2;
+      const char* src = reinterpret_cast<const char*>(src0 + (int64_t)p0 * piece_words);
+      char* d = reinterpret_cast<char*>(dst);
+      for (int i = tid; i < n16; i += kNCT) cp_async_16_plain(d + i * 16, src + (int64_t)i * 16);
+      cp_async_commit_wait_all();
+      consumer_sync(kNCT);
     };
     // folds pieces [p0, p0 + n) of the shared-memory chunk into item idx's state
     auto fold_chunk = [&](int idx, int p0, int n, float4& O, float& M, float& L) {

@@ -430,21 +430,15 @@ __device__ __forceinline__ void st_relaxed_gpu_s32(int32_t* p, int32_t v) {
   asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Bulk (non-tensor) copy global -> shared without a cache hint (piece words
-// of the split-KV merge, which stay in L2).
-__device__ __forceinline__ void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes,
-                                               uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
+// 16-byte cp.async (L2 only) global -> shared without a cache hint: the
+// piece words of the split-KV merge, read by the generic proxy like the
+// stores that wrote them.
+__device__ __forceinline__ void cp_async_16_plain(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
 }
-
-// Orders this thread's generic-proxy accesses before its later async-proxy
-// (bulk copy) accesses of global memory.
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
+__device__ __forceinline__ void cp_async_commit_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
 // System-scope 64-bit accesses for the peer exchange (another GPU's kernel
