@@ -868,6 +868,8 @@ enum TraceSlot : int {
   kTrProdLast = 9,   // producer: last copy issued
   kTrInfo = 10,      // tiles | early tiles << 16 | merger << 24 | smid << 32
   kTrExit = 11,      // consumers done
+  kTrGather = 12,    // merger: first chunk of pieces copied into shared memory
+  kTrFolded = 13,    // merger: every piece folded (before the result is written)
 };
 
 // ---------------------------------------------------------------------------
@@ -1411,164 +1413,175 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
     return (uint64_t)__float_as_uint(v) | ((uint64_t)ep << 32);
   };
   auto fresh = [](uint64_t w, uint32_t ep) { return (uint32_t)(w >> 32) == ep; };
-  // Piece words of head h, columns d..d+3 (o), and (m, l) polled from global
-  // memory until they carry epoch ep (bounded).
-  auto poll_piece = [&](const uint64_t* row, int d, uint32_t ep, uint64_t (&w)[6]) {
+  constexpr int kD4 = HD / 4;  // float4 column chunks of a head row
+  // A piece word polled from global memory until it carries epoch ep
+  // (bounded: a piece that never arrives latches GLA_ERR_TIMEOUT).
+  auto poll_word = [&](const uint64_t* p, uint32_t ep) -> uint64_t {
     unsigned long long t0 = 0;
     for (;;) {
-      ld_relaxed_gpu_u64x2(row + d, w[0], w[1]);
-      ld_relaxed_gpu_u64x2(row + d + 2, w[2], w[3]);
-      ld_relaxed_gpu_u64x2(row + HD, w[4], w[5]);
-      bool ok = true;
-#pragma unroll
-      for (int e = 0; e < 6; ++e) ok = ok && fresh(w[e], ep);
-      if (ok || flags[0]) return;
+      uint64_t w0, w1;
+      ld_relaxed_gpu_u64x2(
+          reinterpret_cast<const uint64_t*>(reinterpret_cast<uintptr_t>(p) & ~(uintptr_t)15), w0,
+          w1);
+      const uint64_t w = (reinterpret_cast<uintptr_t>(p) & 8) ? w1 : w0;
+      if (fresh(w, ep) || flags[0]) return w;
       if (t0 == 0) {
         t0 = global_timer_ns();
       } else if (global_timer_ns() - t0 > kWaitTimeoutNs) {
         flags[0] = 1;
         atomicCAS(a.status, 0, GLA_ERR_TIMEOUT);
-        return;
+        return w;
       }
     }
   };
-  // Running log-sum-exp fold of one piece (log2-domain m) into (O, M, L).
-  auto fold = [&](float4& O, float& M, float& L, const uint64_t (&w)[6]) {
-    const float m = __uint_as_float((uint32_t)w[4]);
-    if (m == -INFINITY) return;  // an empty piece
-    const float l = __uint_as_float((uint32_t)w[5]);
-    const float Mn = fmaxf(M, m);
-    const float sa = (M == -INFINITY) ? 0.f : fast_exp2(M - Mn);
-    const float sb = fast_exp2(m - Mn);
-    O.x = O.x * sa + sb * __uint_as_float((uint32_t)w[0]);
-    O.y = O.y * sa + sb * __uint_as_float((uint32_t)w[1]);
-    O.z = O.z * sa + sb * __uint_as_float((uint32_t)w[2]);
-    O.w = O.w * sa + sb * __uint_as_float((uint32_t)w[3]);
-    L = L * sa + sb * l;
-    M = Mn;
-  };
-  auto join = [&](float4& O, float& M, float& L, int tpi) {
-    for (int off = 1; off < tpi; off <<= 1) {
-      const float Mo = __shfl_xor_sync(0xffffffffu, M, off);
-      const float Lo = __shfl_xor_sync(0xffffffffu, L, off);
-      float4 Oo;
-      Oo.x = __shfl_xor_sync(0xffffffffu, O.x, off);
-      Oo.y = __shfl_xor_sync(0xffffffffu, O.y, off);
-      Oo.z = __shfl_xor_sync(0xffffffffu, O.z, off);
-      Oo.w = __shfl_xor_sync(0xffffffffu, O.w, off);
-      const float Mn = fmaxf(M, Mo);
-      const float sa = (M == -INFINITY) ? 0.f : fast_exp2(M - Mn);
-      const float sb = (Mo == -INFINITY) ? 0.f : fast_exp2(Mo - Mn);
-      O.x = O.x * sa + Oo.x * sb; O.y = O.y * sa + Oo.y * sb;
-      O.z = O.z * sa + Oo.z * sb; O.w = O.w * sa + Oo.w * sb;
-      L = L * sa + Lo * sb;
-      M = Mn;
-    }
-  };
-  // Items (head, 4 columns) of the merge and the threads that share one.
-  constexpr int kD4 = HD / 4;
-  constexpr int kIPT = (kMaxGroup * kD4 + kNCT - 1) / kNCT;  // item passes a thread
-  auto merge_shape = [&](int* tpi) {
-    const int items = G * kD4;
-    int t = 1;
-    while (t < 8 && items * t * 2 <= kNCT) t *= 2;
-    *tpi = t;
-    return items;
-  };
+  auto lo_f = [](uint64_t w) { return __uint_as_float((uint32_t)w); };
 
   // Merger: the segment's slots c0 + s .. c0 + s + npieces - 1 (consecutive)
   // are copied into shared memory `dst` (the drained ring, or the warp merge
   // buffer when the ring still holds this CTA's next piece) in chunks of
-  // whole pieces; every thread folds its items' pieces from there (words a
-  // piece's CTA has not stored yet are polled again from global memory).
+  // whole pieces.  Per chunk, one warp per q head turns the pieces' (m, l)
+  // into weights e = 2^(m - M) (M the running maximum; the running state is
+  // rescaled when it grows) and the sum of e l; then every thread adds e o
+  // over the pieces for 16-byte column pairs of the [G][HD] result
+  // (consecutive threads read consecutive words: no bank conflicts, no exp2
+  // in the inner loop).  A word a piece's CTA had not stored yet at the copy
+  // is polled again from global memory.
   auto gather = [&](int b, int g, int s, int c0, int npieces, uint32_t ep, char* dst_bytes,
                     int cap_bytes) {
-    int tpi;
-    const int items = merge_shape(&tpi);
     const int piece_words = G * kSH;
+    const int piece_bytes = piece_words * 8;
     const uint64_t* src0 = a.ws_part + (int64_t)(c0 + s) * piece_words;
-    const int cap = imin(npieces, cap_bytes / (piece_words * 8));
-    uint64_t* dst = reinterpret_cast<uint64_t*>(dst_bytes);
+    const int cap =
+        imin(npieces, (cap_bytes - 3 * kMaxGroup * 4) / (piece_bytes + kMaxGroup * 4));
+    const uint64_t* dst = reinterpret_cast<const uint64_t*>(dst_bytes);
+    float* E = reinterpret_cast<float*>(dst_bytes + (size_t)cap * piece_bytes);  // [cap][G]
+    float* Mh = E + cap * G;     // [G] running max (log2 units)
+    float* Lh = Mh + kMaxGroup;  // [G] running sum of the l weights
+    float* Sh = Lh + kMaxGroup;  // [G] rescale of the running state by this chunk
     // early copies that the true length did not need may still be landing in
     // the ring: the producer drains them, and so does the merger before it
     // overwrites the ring
     if (tid == 0 && dst_bytes == smem)
       for (int k = my_tiles; k < flags[5]; ++k) mbar_wait(&land[k], 0, flags, a.status);
+    constexpr int kHalf = HD / 2;
+    const int nq = G * kHalf;  // column pairs of the result
     // every consumer thread copies its share of the chunk's 16-byte words
     // (cp.async: no registers, all copies in flight at once)
     auto copy_chunk = [&](int p0, int n) {
       const int n16 = n * piece_words / 2;
       const char* src = reinterpret_cast<const char*>(src0 + (int64_t)p0 * piece_words);
-      char* d = reinterpret_cast<char*>(dst);
-      for (int i = tid; i < n16; i += kNCT) cp_async_16_plain(d + i * 16, src + (int64_t)i * 16);
+      for (int i = tid; i < n16; i += kNCT) cp_async_16_plain(dst_bytes + i * 16, src + (int64_t)i * 16);
       cp_async_commit_wait_all();
       consumer_sync(kNCT);
+      if (p0 == 0 && tid == 0) stamp(kTrGather);
     };
-    // folds pieces [p0, p0 + n) of the shared-memory chunk into item idx's state
-    auto fold_chunk = [&](int idx, int p0, int n, float4& O, float& M, float& L) {
-      const bool active = idx < items * tpi;
-      const int it = active ? idx / tpi : 0, j = idx % tpi;
-      const int h = it / kD4, d = (it - h * kD4) * 4;
-      if (!active) return;
-      for (int pi = j; pi < n; pi += tpi) {
-        const uint64_t* row = dst + ((int64_t)pi * G + h) * kSH;
-        uint64_t w[6];
-        const ulonglong2 w01 = *reinterpret_cast<const ulonglong2*>(row + d);
-        const ulonglong2 w23 = *reinterpret_cast<const ulonglong2*>(row + d + 2);
-        const ulonglong2 w45 = *reinterpret_cast<const ulonglong2*>(row + HD);
-        w[0] = w01.x; w[1] = w01.y; w[2] = w23.x; w[3] = w23.y; w[4] = w45.x; w[5] = w45.y;
-        bool ok = true;
-#pragma unroll
-        for (int e = 0; e < 6; ++e) ok = ok && fresh(w[e], ep);
-        if (!ok) poll_piece(src0 + ((int64_t)(p0 + pi) * G + h) * kSH, d, ep, w);
-        fold(O, M, L, w);
+    // weights of pieces [p0, p0 + n): warp w takes q heads w, w + NW, ...
+    auto weights = [&](int p0, int n) {
+      if (p0 == 0 && tid < G) {
+        Mh[tid] = -INFINITY;
+        Lh[tid] = 0.f;
       }
-    };
-    auto finish_item = [&](int idx, float4& O, float& M, float& L) {
-      const bool active = idx < items * tpi;
-      const int it = active ? idx / tpi : 0, j = idx % tpi;
-      const int h = it / kD4, d = (it - h * kD4) * 4;
-      join(O, M, L, tpi);
-      if (active && j == 0) write_final4<HD, XCH>(a, b, g * G + h, d, O, M, L, (uint32_t)flags[2]);
-    };
-    if constexpr (LOADER == 1) {
-      // register-lean (two CTAs an SM): one item pass at a time; the chunks
-      // are copied again for every pass unless all pieces fit in one
-      const bool one_chunk = cap >= npieces;
-      if (one_chunk) copy_chunk(0, npieces);
-      for (int base = 0; base < items * tpi; base += kNCT) {  // warp-uniform trip count
-        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-        float M = -INFINITY, L = 0.f;
-        for (int p0 = 0; p0 < npieces; p0 += cap) {
-          const int n = imin(cap, npieces - p0);
-          if (!one_chunk) copy_chunk(p0, n);
-          fold_chunk(base + tid, p0, n, O, M, L);
-          if (!one_chunk) consumer_sync(kNCT);  // the chunk is read before the next one lands
+      consumer_sync(kNCT);
+      for (int h = warp; h < G; h += NW) {
+        auto ml = [&](int p, int k) {  // word HD + k (0: m, 1: l) of piece p, head h
+          const uint64_t w = dst[((int64_t)p * G + h) * kSH + HD + k];
+          return fresh(w, ep) ? w
+                              : poll_word(src0 + ((int64_t)(p0 + p) * G + h) * kSH + HD + k, ep);
+        };
+        float mx = -INFINITY;
+        for (int p = lane; p < n; p += 32) mx = fmaxf(mx, lo_f(ml(p, 0)));
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        const float Mold = Mh[h];
+        const float Mn = fmaxf(Mold, mx);
+        float ls = 0.f;
+        for (int p = lane; p < n; p += 32) {
+          const float m = lo_f(ml(p, 0));
+          const float e = (m == -INFINITY) ? 0.f : fast_exp2(m - Mn);
+          E[p * G + h] = e;
+          ls = fmaf(e, lo_f(ml(p, 1)), ls);
         }
-        finish_item(base + tid, O, M, L);
-      }
-      if (one_chunk) consumer_sync(kNCT);
-    } else {
-      float4 O[kIPT];
-      float M[kIPT], L[kIPT];
 #pragma unroll
-      for (int ip = 0; ip < kIPT; ++ip) {
-        O[ip] = make_float4(0.f, 0.f, 0.f, 0.f);
-        M[ip] = -INFINITY;
-        L[ip] = 0.f;
+        for (int off = 16; off >= 1; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+        __syncwarp();
+        if (lane == 0) {
+          const float so = (Mold == -INFINITY) ? 0.f : fast_exp2(Mold - Mn);
+          Sh[h] = so;
+          Mh[h] = Mn;
+          Lh[h] = Lh[h] * so + ls;
+        }
       }
+      consumer_sync(kNCT);
+    };
+    // column pair q of the result over pieces [p0, p0 + n), added to r
+    auto sums = [&](int q, int p0, int n, float2& r) {
+      const int h = q / kHalf, c = (q - h * kHalf) * 2;
+      const float sc = Sh[h];
+      r.x *= sc;
+      r.y *= sc;
+      const uint64_t* col = dst + (int64_t)h * kSH + c;
+      const float* eh = E + h;
+#pragma unroll 4
+      for (int p = 0; p < n; ++p) {
+        ulonglong2 w = *reinterpret_cast<const ulonglong2*>(col + (int64_t)p * piece_words);
+        if (!fresh(w.x, ep) || !fresh(w.y, ep)) {
+          const uint64_t* gw = src0 + ((int64_t)(p0 + p) * G + h) * kSH + c;
+          w.x = poll_word(gw, ep);
+          w.y = poll_word(gw + 1, ep);
+        }
+        const float e = eh[p * G];
+        r.x = fmaf(e, lo_f(w.x), r.x);
+        r.y = fmaf(e, lo_f(w.y), r.y);
+      }
+    };
+    auto write_pair = [&](int q, const float2& r) {
+      const int h = q / kHalf, c = (q - h * kHalf) * 2;
+      const float M = Mh[h], L = Lh[h];
+      write_final<HD, XCH>(a, b, g * G + h, c, r.x, M, L, (uint32_t)flags[2]);
+      write_final<HD, XCH>(a, b, g * G + h, c + 1, r.y, M, L, (uint32_t)flags[2]);
+    };
+    constexpr int kQ = (kMaxGroup * kHalf + kNCT - 1) / kNCT;  // column pairs a thread
+    if constexpr (LOADER == 0) {
+      // one CTA an SM (registers to spare): chunks outermost, each copied once
+      float2 acc[kQ];
+#pragma unroll
+      for (int i = 0; i < kQ; ++i) acc[i] = make_float2(0.f, 0.f);
       for (int p0 = 0; p0 < npieces; p0 += cap) {
         const int n = imin(cap, npieces - p0);
         copy_chunk(p0, n);
+        weights(p0, n);
 #pragma unroll
-        for (int ip = 0; ip < kIPT; ++ip) fold_chunk(tid + ip * kNCT, p0, n, O[ip], M[ip], L[ip]);
+        for (int i = 0; i < kQ; ++i)
+          if (tid + i * kNCT < nq) sums(tid + i * kNCT, p0, n, acc[i]);
         consumer_sync(kNCT);  // the chunk is read before the next one lands
       }
+      if (tid == 0) stamp(kTrFolded);
 #pragma unroll
-      for (int ip = 0; ip < kIPT; ++ip) {
-        if (ip * kNCT >= items * tpi) break;  // warp-uniform: no thread of this pass is active
-        finish_item(tid + ip * kNCT, O[ip], M[ip], L[ip]);
+      for (int i = 0; i < kQ; ++i)
+        if (tid + i * kNCT < nq) write_pair(tid + i * kNCT, acc[i]);
+    } else {
+      // register-lean (two CTAs an SM): one column pair at a time; the chunks
+      // are copied again for every pass unless all pieces fit in one
+      const bool one_chunk = cap >= npieces;
+      if (one_chunk) {
+        copy_chunk(0, npieces);
+        weights(0, npieces);
       }
+#pragma unroll 1
+      for (int i = 0; i < kQ; ++i) {
+        float2 r = make_float2(0.f, 0.f);
+        for (int p0 = 0; p0 < npieces; p0 += cap) {
+          const int n = imin(cap, npieces - p0);
+          if (!one_chunk) {
+            copy_chunk(p0, n);
+            weights(p0, n);
+          }
+          if (tid + i * kNCT < nq) sums(tid + i * kNCT, p0, n, r);
+          if (!one_chunk) consumer_sync(kNCT);  // the chunk is read before the next one lands
+        }
+        if (tid + i * kNCT < nq) write_pair(tid + i * kNCT, r);
+      }
+      consumer_sync(kNCT);
     }
   };
 
