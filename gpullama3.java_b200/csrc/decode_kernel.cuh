@@ -870,6 +870,8 @@ enum TraceSlot : int {
   kTrExit = 11,      // consumers done
   kTrGather = 12,    // merger: first chunk of pieces copied into shared memory
   kTrFolded = 13,    // merger: every piece folded (before the result is written)
+  kTrMergeCycles = 14,  // merger, first head: SM cycles of copy | weights | sums | rest (16 bits each)
+  kTrMergeTries = 15,   // merger, first head: copy rounds
 };
 
 // ---------------------------------------------------------------------------
@@ -1280,17 +1282,21 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
     if (XCH && tid == 0)
       flags[2] = (int)(*reinterpret_cast<volatile uint32_t*>(a.xch_local + xch_epoch_offset(g)) + 1u);
   };
-  auto publish_merge = [&](int g) {
+  // Merger r of nm (see finish_piece) publishes q heads r, r + nm, ... of
+  // kv head g; merger 0 (the last to count) advances g's epoch.
+  auto publish_merge = [&](int g, int r, int nm) {
     if constexpr (!XCH) return;
     const uint32_t ep = (uint32_t)flags[2];
     const int par = (int)(ep & 1u), W = a.xch_world;
-    if (tid == 0) *reinterpret_cast<volatile uint32_t*>(a.xch_local + xch_epoch_offset(g)) = ep;
+    if (tid == 0 && r == 0)
+      *reinterpret_cast<volatile uint32_t*>(a.xch_local + xch_epoch_offset(g)) = ep;
     constexpr int kXR = xch_row_floats<HD>();
     constexpr int kD4 = HD / 4;
     // ranks polled together (bounds the registers; the FP32 kernels have fewer)
     constexpr int kRG = Consumer::kElemBytes == 2 ? 4 : 2;
-    for (int it = tid; it < G * kD4; it += kNCT) {
-      const int hq = g * G + it / kD4, d = (it % kD4) * 4;
+    const int n_heads_mine = (G - r + nm - 1) / nm;
+    for (int it = tid; it < n_heads_mine * kD4; it += kNCT) {
+      const int hq = g * G + r + (it / kD4) * nm, d = (it % kD4) * 4;
       float M = -INFINITY, L = 0.f;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int r0 = 0; r0 < W; r0 += kRG) {
@@ -1353,7 +1359,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
       consumer_sync(kNCT);
       for (int idx = tid; idx < G * HD; idx += kNCT)
         write_final<HD, XCH>(a, b, g * G + idx / HD, idx % HD, 0.f, 0.f, 0.f, (uint32_t)flags[2]);
-      if constexpr (XCH) publish_merge(g);
+      if constexpr (XCH) publish_merge(g, 0, 1);
     }
   }
   const CtaTiles ct = cta_tiles();
@@ -1436,150 +1442,169 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
   };
   auto lo_f = [](uint64_t w) { return __uint_as_float((uint32_t)w); };
 
-  // Merger: the segment's slots c0 + s .. c0 + s + npieces - 1 (consecutive)
-  // are copied into shared memory `dst` (the drained ring, or the warp merge
-  // buffer when the ring still holds this CTA's next piece) in chunks of
-  // whole pieces.  Per chunk, one warp per q head turns the pieces' (m, l)
-  // into weights e = 2^(m - M) (M the running maximum; the running state is
-  // rescaled when it grows) and the sum of e l; then every thread adds e o
-  // over the pieces for 16-byte column pairs of the [G][HD] result
-  // (consecutive threads read consecutive words: no bank conflicts, no exp2
-  // in the inner loop).  A word a piece's CTA had not stored yet at the copy
-  // is polled again from global memory.
-  auto gather = [&](int b, int g, int s, int c0, int npieces, uint32_t ep, char* dst_bytes,
-                    int cap_bytes) {
+  // Split-KV merge of segment s.  The last nm = min(G, npieces) CTAs to
+  // count are its mergers: merger r (r = 0 the very last) merges q heads r,
+  // r + nm, ... so the merge runs on nm SMs at once.  For each of its heads a
+  // merger copies that head's row (o, m, l) of every piece into shared memory
+  // `buf` (the drained ring, or the warp merge buffer when the ring still
+  // holds this CTA's next piece; chunks of whole pieces when they do not
+  // fit).  Every warp then turns the pieces' (m, l) into weights e = 2^(m - M)
+  // (M the running maximum) and the sum of e l - the same values in every
+  // warp, so no barrier sits between weights and sums - and every thread adds
+  // e o over its share of the pieces for a pair of columns.  The epochs are
+  // checked on the words as they are used; if any word was stale (a piece
+  // whose CTA had not stored yet), the chunk is copied again and redone
+  // (bounded).
+  auto merge_heads = [&](int b, int g, int s, int c0, int npieces, uint32_t ep, int r, int nm,
+                         char* buf, int cap_bytes) {
+    constexpr int kRowW = HD + 4;       // words of a head row: o[HD], m, l, 2 pad
+    constexpr int kRowB = kRowW * 8;
+    constexpr int kC16 = kRowB / 16;    // 16-byte chunks of a row
+    constexpr int kHalf = HD / 2;       // column pairs
+    constexpr int kTPI = kNCT / kHalf;  // threads per column pair (piece split)
+    // pieces a lane holds in the weights (a chunk has at most 32 kPL pieces;
+    // fewer registers in the two-CTA kernels, whose segments have few pieces)
+    constexpr int kPL = LOADER == 0 ? 6 : 2;
     const int piece_words = G * kSH;
-    const int piece_bytes = piece_words * 8;
     const uint64_t* src0 = a.ws_part + (int64_t)(c0 + s) * piece_words;
-    const int cap =
-        imin(npieces, (cap_bytes - 3 * kMaxGroup * 4) / (piece_bytes + kMaxGroup * 4));
-    const uint64_t* dst = reinterpret_cast<const uint64_t*>(dst_bytes);
-    float* E = reinterpret_cast<float*>(dst_bytes + (size_t)cap * piece_bytes);  // [cap][G]
-    float* Mh = E + cap * G;     // [G] running max (log2 units)
-    float* Lh = Mh + kMaxGroup;  // [G] running sum of the l weights
-    float* Sh = Lh + kMaxGroup;  // [G] rescale of the running state by this chunk
+    // buf: rows [cap][kRowW] words, then each warp's weights [NW][cap]; the
+    // [kTPI][HD] partial sums reuse the rows once the pieces are folded
+    // (kTPI * HD * 4 <= 2 KB)
+    const int cap = imin(imin(npieces, 32 * kPL), cap_bytes / (kRowB + NW * 4));
+    char* rows = buf;
+    float* Ew = reinterpret_cast<float*>(buf + (size_t)cap * kRowB) + warp * cap;
+    float* part = reinterpret_cast<float*>(buf);
     // early copies that the true length did not need may still be landing in
     // the ring: the producer drains them, and so does the merger before it
     // overwrites the ring
-    if (tid == 0 && dst_bytes == smem)
+    if (tid == 0 && buf == smem)
       for (int k = my_tiles; k < flags[5]; ++k) mbar_wait(&land[k], 0, flags, a.status);
-    constexpr int kHalf = HD / 2;
-    const int nq = G * kHalf;  // column pairs of the result
-    // every consumer thread copies its share of the chunk's 16-byte words
-    // (cp.async: no registers, all copies in flight at once)
-    auto copy_chunk = [&](int p0, int n) {
-      const int n16 = n * piece_words / 2;
-      const char* src = reinterpret_cast<const char*>(src0 + (int64_t)p0 * piece_words);
-      for (int i = tid; i < n16; i += kNCT) cp_async_16_plain(dst_bytes + i * 16, src + (int64_t)i * 16);
-      cp_async_commit_wait_all();
-      consumer_sync(kNCT);
-      if (p0 == 0 && tid == 0) stamp(kTrGather);
-    };
-    // weights of pieces [p0, p0 + n): warp w takes q heads w, w + NW, ...
-    auto weights = [&](int p0, int n) {
-      if (p0 == 0 && tid < G) {
-        Mh[tid] = -INFINITY;
-        Lh[tid] = 0.f;
-      }
-      consumer_sync(kNCT);
-      for (int h = warp; h < G; h += NW) {
-        auto ml = [&](int p, int k) {  // word HD + k (0: m, 1: l) of piece p, head h
-          const uint64_t w = dst[((int64_t)p * G + h) * kSH + HD + k];
-          return fresh(w, ep) ? w
-                              : poll_word(src0 + ((int64_t)(p0 + p) * G + h) * kSH + HD + k, ep);
-        };
-        float mx = -INFINITY;
-        for (int p = lane; p < n; p += 32) mx = fmaxf(mx, lo_f(ml(p, 0)));
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-        const float Mold = Mh[h];
-        const float Mn = fmaxf(Mold, mx);
-        float ls = 0.f;
-        for (int p = lane; p < n; p += 32) {
-          const float m = lo_f(ml(p, 0));
-          const float e = (m == -INFINITY) ? 0.f : fast_exp2(m - Mn);
-          E[p * G + h] = e;
-          ls = fmaf(e, lo_f(ml(p, 1)), ls);
-        }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
-        __syncwarp();
-        if (lane == 0) {
-          const float so = (Mold == -INFINITY) ? 0.f : fast_exp2(Mold - Mn);
-          Sh[h] = so;
-          Mh[h] = Mn;
-          Lh[h] = Lh[h] * so + ls;
-        }
-      }
-      consumer_sync(kNCT);
-    };
-    // column pair q of the result over pieces [p0, p0 + n), added to r
-    auto sums = [&](int q, int p0, int n, float2& r) {
-      const int h = q / kHalf, c = (q - h * kHalf) * 2;
-      const float sc = Sh[h];
-      r.x *= sc;
-      r.y *= sc;
-      const uint64_t* col = dst + (int64_t)h * kSH + c;
-      const float* eh = E + h;
-#pragma unroll 4
-      for (int p = 0; p < n; ++p) {
-        ulonglong2 w = *reinterpret_cast<const ulonglong2*>(col + (int64_t)p * piece_words);
-        if (!fresh(w.x, ep) || !fresh(w.y, ep)) {
-          const uint64_t* gw = src0 + ((int64_t)(p0 + p) * G + h) * kSH + c;
-          w.x = poll_word(gw, ep);
-          w.y = poll_word(gw + 1, ep);
-        }
-        const float e = eh[p * G];
-        r.x = fmaf(e, lo_f(w.x), r.x);
-        r.y = fmaf(e, lo_f(w.y), r.y);
-      }
-    };
-    auto write_pair = [&](int q, const float2& r) {
-      const int h = q / kHalf, c = (q - h * kHalf) * 2;
-      const float M = Mh[h], L = Lh[h];
-      write_final<HD, XCH>(a, b, g * G + h, c, r.x, M, L, (uint32_t)flags[2]);
-      write_final<HD, XCH>(a, b, g * G + h, c + 1, r.y, M, L, (uint32_t)flags[2]);
-    };
-    constexpr int kQ = (kMaxGroup * kHalf + kNCT - 1) / kNCT;  // column pairs a thread
-    if constexpr (LOADER == 0) {
-      // one CTA an SM (registers to spare): chunks outermost, each copied once
-      float2 acc[kQ];
-#pragma unroll
-      for (int i = 0; i < kQ; ++i) acc[i] = make_float2(0.f, 0.f);
+    const int q = tid % kHalf, j = tid / kHalf;  // column pair, piece share
+    const bool active = j < kTPI;
+    long long ck[5] = {clock64(), 0, 0, 0, 0};
+    int tries = 0;
+    for (int h = r; h < G; h += nm) {
+      float2 acc = make_float2(0.f, 0.f);
+      float Mrun = -INFINITY, Lrun = 0.f;
       for (int p0 = 0; p0 < npieces; p0 += cap) {
         const int n = imin(cap, npieces - p0);
-        copy_chunk(p0, n);
-        weights(p0, n);
-#pragma unroll
-        for (int i = 0; i < kQ; ++i)
-          if (tid + i * kNCT < nq) sums(tid + i * kNCT, p0, n, acc[i]);
-        consumer_sync(kNCT);  // the chunk is read before the next one lands
-      }
-      if (tid == 0) stamp(kTrFolded);
-#pragma unroll
-      for (int i = 0; i < kQ; ++i)
-        if (tid + i * kNCT < nq) write_pair(tid + i * kNCT, acc[i]);
-    } else {
-      // register-lean (two CTAs an SM): one column pair at a time; the chunks
-      // are copied again for every pass unless all pieces fit in one
-      const bool one_chunk = cap >= npieces;
-      if (one_chunk) {
-        copy_chunk(0, npieces);
-        weights(0, npieces);
-      }
-#pragma unroll 1
-      for (int i = 0; i < kQ; ++i) {
-        float2 r = make_float2(0.f, 0.f);
-        for (int p0 = 0; p0 < npieces; p0 += cap) {
-          const int n = imin(cap, npieces - p0);
-          if (!one_chunk) {
-            copy_chunk(p0, n);
-            weights(p0, n);
+        unsigned long long t0 = 0;
+        for (;;) {  // until every word of the chunk carried the epoch
+          for (int i = tid; i < n * kC16; i += kNCT) {
+            const int p = i / kC16, c = i - p * kC16;
+            cp_async_16_plain(rows + (size_t)p * kRowB + c * 16,
+                              reinterpret_cast<const char*>(
+                                  src0 + ((int64_t)(p0 + p) * G + h) * kSH) + c * 16);
           }
-          if (tid + i * kNCT < nq) sums(tid + i * kNCT, p0, n, r);
-          if (!one_chunk) consumer_sync(kNCT);  // the chunk is read before the next one lands
+          cp_async_commit_wait_all();
+          consumer_sync(kNCT);
+          ++tries;
+          if (tries == 1) ck[1] = clock64();
+          if (p0 == 0 && h == r && tid == 0) stamp(kTrGather);
+          // weights, computed by every warp: lane holds pieces lane + 32 k
+          bool stale = false;
+          float mk[kPL], lk[kPL];
+          float mx = -INFINITY;
+#pragma unroll
+          for (int k = 0; k < kPL; ++k) {
+            const int p = lane + 32 * k;
+            mk[k] = -INFINITY;
+            lk[k] = 0.f;
+            if (p < n) {
+              const ulonglong2 w = lds_u64x2(smem_u32(rows + (size_t)p * kRowB + HD * 8));
+              stale = stale || !fresh(w.x, ep) || !fresh(w.y, ep);
+              mk[k] = lo_f(w.x);
+              lk[k] = lo_f(w.y);
+              mx = fmaxf(mx, mk[k]);
+            }
+          }
+#pragma unroll
+          for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+          const float Mn = fmaxf(Mrun, mx);
+          float ls = 0.f;
+#pragma unroll
+          for (int k = 0; k < kPL; ++k) {
+            const int p = lane + 32 * k;
+            if (p < n) {
+              const float e = (mk[k] == -INFINITY) ? 0.f : fast_exp2(mk[k] - Mn);
+              Ew[p] = e;
+              ls = fmaf(e, lk[k], ls);
+            }
+          }
+#pragma unroll
+          for (int off = 16; off >= 1; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+          const float so = (Mrun == -INFINITY) ? 0.f : fast_exp2(Mrun - Mn);
+          __syncwarp();
+          if (tries == 1) ck[2] = clock64();
+          float2 r2 = make_float2(acc.x * so, acc.y * so);
+          if (active) {
+            const uint32_t col = smem_u32(rows) + (uint32_t)q * 16u;
+            const uint32_t eb = smem_u32(Ew);
+            int p = j;
+            for (; p + 3 * kTPI < n; p += 4 * kTPI) {
+              ulonglong2 w[4];
+              float e[4];
+#pragma unroll
+              for (int u = 0; u < 4; ++u) w[u] = lds_u64x2(col + (uint32_t)(p + u * kTPI) * kRowB);
+#pragma unroll
+              for (int u = 0; u < 4; ++u) e[u] = lds_f32(eb + (uint32_t)(p + u * kTPI) * 4u);
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                stale = stale || !fresh(w[u].x, ep) || !fresh(w[u].y, ep);
+                r2.x = fmaf(e[u], lo_f(w[u].x), r2.x);
+                r2.y = fmaf(e[u], lo_f(w[u].y), r2.y);
+              }
+            }
+            for (; p < n; p += kTPI) {
+              const ulonglong2 w = lds_u64x2(col + (uint32_t)p * kRowB);
+              const float e = lds_f32(eb + (uint32_t)p * 4u);
+              stale = stale || !fresh(w.x, ep) || !fresh(w.y, ep);
+              r2.x = fmaf(e, lo_f(w.x), r2.x);
+              r2.y = fmaf(e, lo_f(w.y), r2.y);
+            }
+          }
+          if (tries == 1) ck[3] = clock64();
+          // the chunk is read before it is copied again or the next one lands
+          const bool any_stale = consumer_sync_or(kNCT, stale);
+          if (!any_stale || flags[0]) {
+            acc = r2;
+            Lrun = Lrun * so + ls;
+            Mrun = Mn;
+            break;
+          }
+          if (tid == 0) {
+            if (t0 == 0) t0 = global_timer_ns();
+            else if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+              flags[0] = 1;
+              atomicCAS(a.status, 0, GLA_ERR_TIMEOUT);
+            }
+          }
         }
-        if (tid + i * kNCT < nq) write_pair(tid + i * kNCT, r);
+      }
+      if (h == r) {
+        ck[4] = clock64();
+        if (a.trace && tid == 0) {
+          auto d16 = [](long long x) { return (uint64_t)(x > 65535 ? 65535 : x); };
+          a.trace[(size_t)blockIdx.x * kTraceWords + kTrMergeCycles] =
+              d16(ck[1] - ck[0]) | (d16(ck[2] - ck[1]) << 16) | (d16(ck[3] - ck[2]) << 32) |
+              (d16(ck[4] - ck[3]) << 48);
+          a.trace[(size_t)blockIdx.x * kTraceWords + kTrMergeTries] = (uint64_t)tries;
+        }
+      }
+      // join the kTPI shares of every column pair and write the head
+      if (active) *reinterpret_cast<float2*>(part + j * HD + 2 * q) = acc;
+      consumer_sync(kNCT);
+      if (tid == 0) stamp(kTrFolded);
+      if (tid < kHalf) {
+        float2 t = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < kTPI; ++u) {
+          const float2 v = *reinterpret_cast<const float2*>(part + u * HD + 2 * tid);
+          t.x += v.x;
+          t.y += v.y;
+        }
+        write_final<HD, XCH>(a, b, g * G + h, 2 * tid, t.x, Mrun, Lrun, (uint32_t)flags[2]);
+        write_final<HD, XCH>(a, b, g * G + h, 2 * tid + 1, t.y, Mrun, Lrun, (uint32_t)flags[2]);
       }
       consumer_sync(kNCT);
     }
@@ -1625,20 +1650,25 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
         if (d == 0) st_relaxed_gpu_u64x2(slot + HD, tag(M, ep), tag(L, ep));
       }
     }
-    bool merged_here = npieces == 1;  // this CTA holds the segment's final records
+    bool merged_here = npieces == 1;  // this CTA writes final records of the segment
+    int mr = 0, mn = 1;                 // merger index and mergers of the segment
     if (npieces > 1) {
       consumer_sync(kNCT);
-      if (tid == 0) {
-        const int old = atomic_add_relaxed_gpu(&a.ws_counter[s], 1);
-        flags[1] = (old == npieces - 1) ? 1 : 0;
-      }
+      if (tid == 0) flags[1] = atomic_add_relaxed_gpu(&a.ws_counter[s], 1);
       consumer_sync(kNCT);
-      merged_here = flags[1] != 0;
+      // round robin: the last G to count merge (each CTA holds one piece, so
+      // a merger that waits for a later piece holds up no other segment);
+      // contiguous deal: only the last, which never waits for a piece (an
+      // earlier merger would wait for CTAs still busy with earlier segments)
+      mn = deal.mode == 1 ? imin(G, npieces) : 1;
+      mr = npieces - 1 - flags[1];  // 0: the last to count
+      merged_here = mr < mn;
       if (tid == 0) stamp(kTrCounted);
       if (merged_here) {
-        if (ring_free) gather(b, g, s, c0, npieces, ep, smem, a.stages * a.stage_bytes);
-        else gather(b, g, s, c0, npieces, ep, reinterpret_cast<char*>(merge), kMergeBytes);
-        if (tid == 0) st_relaxed_gpu_s32(&a.ws_counter[s], 0);
+        if (ring_free) merge_heads(b, g, s, c0, npieces, ep, mr, mn, smem, a.stages * a.stage_bytes);
+        else merge_heads(b, g, s, c0, npieces, ep, mr, mn, reinterpret_cast<char*>(merge), kMergeBytes);
+        // every CTA has counted: the last one resets the counter
+        if (mr == 0 && tid == 0) st_relaxed_gpu_s32(&a.ws_counter[s], 0);
       }
     } else if (tid == 0) {
       stamp(kTrCounted);
@@ -1646,7 +1676,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
     consumer_sync(kNCT);
     if (merged_here && tid == 0) stamp(kTrMerged);
     if constexpr (XCH) {
-      if (merged_here) publish_merge(g);
+      if (merged_here) publish_merge(g, mr, mn);
     }
     if (merged_here && tid == 0) stamp(kTrPublished);
     return merged_here;

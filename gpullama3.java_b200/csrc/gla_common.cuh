@@ -385,6 +385,21 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   return p;
 }
 
+// Named barrier 1 over the consumer threads that also ORs a predicate across
+// them: true if any thread passed true.
+__device__ __forceinline__ bool consumer_sync_or(int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // Named barrier over the `nthreads` consumer threads (id 1; id 0 is
 // __syncthreads).
 __device__ __forceinline__ void consumer_sync(int nthreads) {
@@ -436,6 +451,19 @@ __device__ __forceinline__ void st_relaxed_gpu_s32(int32_t* p, int32_t v) {
 __device__ __forceinline__ void cp_async_16_plain(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
                : "memory");
+}
+// Shared-memory loads by 32-bit shared address (volatile: kept in order with
+// the barriers around them; no memory clobber, so loads of one group issue
+// back to back).
+__device__ __forceinline__ ulonglong2 lds_u64x2(uint32_t addr) {
+  ulonglong2 v;
+  asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
 }
 __device__ __forceinline__ void cp_async_commit_wait_all() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");

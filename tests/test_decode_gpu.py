@@ -442,8 +442,9 @@ def test_decode_after_foreign_pdl_position_update(gla_ctx, oracle, delta, fused)
 def test_phase_trace_option(gla_ctx):
     """GLA_OPT_TRACE: every CTA of the last decode launch leaves ordered
     %globaltimer stamps; the tiles it reports add up to the launch's tiles
-    (C2 layer shape: 8 kv heads x 64 tiles) and exactly one CTA a kv head
-    merges (more than one CTA per kv head hold a piece)."""
+    (C2 layer shape: 8 kv heads x 64 tiles) and, with more than one CTA per
+    kv head holding a piece, the last G CTAs of a kv head to finish merge it
+    (one q head each: 8 kv heads x 3)."""
     import gpullama_attn as gla
 
     torch = _torch()
@@ -464,7 +465,7 @@ def test_phase_trace_option(gla_ctx):
     tiles = (info & 0xFFFF).astype(np.int64)
     merger = (info >> 24) & 0xFF
     assert int(tiles.sum()) == nkv * (n // 64)
-    assert int(merger.sum()) == nkv
+    assert int(merger.sum()) == nkv * (nh // nkv)
     work = tiles > 0
     for col_a, col_b in ((0, 1), (1, 2), (2, 3), (3, 4), (4, 5), (5, 11)):
         assert np.all(tr[work, col_a] <= tr[work, col_b]), (col_a, col_b)
