@@ -100,25 +100,26 @@ int32_t gla_num_sms(const gla_ctx* ctx);
 /* Context options (gla_set_option). */
 #define GLA_OPT_EARLY_KV_PREFETCH 1
 /* GLA_OPT_EARLY_KV_PREFETCH (default 2).  Decode calls launch with
- * programmatic dependent launch and may start reading before the kernel
- * issued just before them on the stream has finished - only if that kernel
- * releases its dependents early (griddepcontrol.launch_dependents); the
- * decode kernels of this library do, and never write caches or positions.
- * (gla_rope_append_f32 also releases its dependents early; it writes q and
- * only the cache row at the position holder, which a following decode over
- * n_pos = position + 1 rows never reads early.)
- * What may be read early:
+ * programmatic dependent launch and may start copying K/V tiles before the
+ * kernel issued just before them on the stream has finished - only if that
+ * kernel releases its dependents early (griddepcontrol.launch_dependents).
+ * Which tiles a CTA copies does not depend on the length (kv head g's tiles
+ * are dealt round robin to its CTA group); the length only bounds how many
+ * are copied early:
  *   1 - calls that take n_pos from the host (gla_decode_*,
- *       gla_decode_partial_*, gla_decode_sharded_*): K/V rows
- *       [0, n_pos - 1), the cache history;
- *   2 - also calls that read positions on the device
- *       (gla_process_heads_flash_attention*, gla_decode_batched_*): the
- *       position holder / n_pos array, then the history rows below it.
- * The newest row (n_pos - 1), q and every other input are read only after
- * the preceding kernel has finished.  0 turns early reads off.  Lower the
- * value if a kernel that runs right before a decode call and releases its
- * dependents early writes older cache rows (use 0) or the positions (use 1).
- * (Early reads apply to the tensor-map loader: single-sequence calls.) */
+ *       gla_decode_partial_*, gla_decode_sharded_*);
+ *   2 - also calls that read the position on the device
+ *       (gla_process_heads_flash_attention*, gla_rope_append_attention_f32),
+ *       which use the position read before the wait only as a hint: copies
+ *       past the true length are dropped, tiles it does not cover are copied
+ *       after the wait.
+ * After the wait the two newest rows [n_pos - 2, n_pos) of every early tile
+ * are read again (or, fused RoPE, the newest written), so a preceding kernel
+ * that releases its dependents early may write the position holder and the
+ * cache rows n_pos - 2 and n_pos - 1 (a KV append, the previous token's fused
+ * append on the same cache); q and the workspace are read after the wait.
+ * Use 0 if such a kernel writes older cache rows.  (Early copies apply to
+ * single-sequence calls.) */
 #define GLA_OPT_COMM_TIMEOUT_MS 3
 /* GLA_OPT_COMM_TIMEOUT_MS (default 60000): host deadline of every step that
  * waits for other ranks - joining the communicator, enqueueing a collective,
