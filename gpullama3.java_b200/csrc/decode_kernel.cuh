@@ -1470,11 +1470,9 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
     // buf: rows [cap][kRowW] words, then each warp's weights [NW][cap]; the
     // [kTPI][HD] partial sums reuse the rows once the pieces are folded
     // (kTPI * HD * 4 <= 2 KB)
-    const int cap = imin(imin(npieces, 32 * kPL), cap_bytes / (kRowB + NW * 4 + 4));
+    const int cap = imin(imin(npieces, 32 * kPL), cap_bytes / (kRowB + NW * 4));
     char* rows = buf;
     float* Ew = reinterpret_cast<float*>(buf + (size_t)cap * kRowB) + warp * cap;
-    // need[p]: the last copy round that found row p stale (0: none)
-    int* need = reinterpret_cast<int*>(buf + (size_t)cap * kRowB) + NW * cap;
     float* part = reinterpret_cast<float*>(buf);
     // early copies that the true length did not need may still be landing in
     // the ring: the producer drains them, and so does the merger before it
@@ -1491,16 +1489,12 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
       for (int p0 = 0; p0 < npieces; p0 += cap) {
         const int n = imin(cap, npieces - p0);
         unsigned long long t0 = 0;
-        for (int p = tid; p < n; p += kNCT) need[p] = 0;
-        consumer_sync(kNCT);
-        for (int round = 1;; ++round) {  // until every word of the chunk carried the epoch
-          // copy the rows found stale in the previous round (all in the first)
+        for (;;) {  // until every word of the chunk carried the epoch
           for (int i = tid; i < n * kC16; i += kNCT) {
             const int p = i / kC16, c = i - p * kC16;
-            if (need[p] == round - 1)
-              cp_async_16_plain(rows + (size_t)p * kRowB + c * 16,
-                                reinterpret_cast<const char*>(
-                                    src0 + ((int64_t)(p0 + p) * G + h) * kSH) + c * 16);
+            cp_async_16_plain(rows + (size_t)p * kRowB + c * 16,
+                              reinterpret_cast<const char*>(
+                                  src0 + ((int64_t)(p0 + p) * G + h) * kSH) + c * 16);
           }
           cp_async_commit_wait_all();
           consumer_sync(kNCT);
@@ -1518,10 +1512,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
             lk[k] = 0.f;
             if (p < n) {
               const ulonglong2 w = lds_u64x2(smem_u32(rows + (size_t)p * kRowB + HD * 8));
-              if (!fresh(w.x, ep) || !fresh(w.y, ep)) {
-                stale = true;
-                need[p] = round;
-              }
+              stale = stale || !fresh(w.x, ep) || !fresh(w.y, ep);
               mk[k] = lo_f(w.x);
               lk[k] = lo_f(w.y);
               mx = fmaxf(mx, mk[k]);
@@ -1559,10 +1550,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
               for (int u = 0; u < 4; ++u) e[u] = lds_f32(eb + (uint32_t)(p + u * kTPI) * 4u);
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
-                if (!fresh(w[u].x, ep) || !fresh(w[u].y, ep)) {
-                  stale = true;
-                  need[p + u * kTPI] = round;
-                }
+                stale = stale || !fresh(w[u].x, ep) || !fresh(w[u].y, ep);
                 r2.x = fmaf(e[u], lo_f(w[u].x), r2.x);
                 r2.y = fmaf(e[u], lo_f(w[u].y), r2.y);
               }
@@ -1570,10 +1558,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
             for (; p < n; p += kTPI) {
               const ulonglong2 w = lds_u64x2(col + (uint32_t)p * kRowB);
               const float e = lds_f32(eb + (uint32_t)p * 4u);
-              if (!fresh(w.x, ep) || !fresh(w.y, ep)) {
-                stale = true;
-                need[p] = round;
-              }
+              stale = stale || !fresh(w.x, ep) || !fresh(w.y, ep);
               r2.x = fmaf(e, lo_f(w.x), r2.x);
               r2.y = fmaf(e, lo_f(w.y), r2.y);
             }
@@ -1594,7 +1579,6 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
               atomicCAS(a.status, 0, GLA_ERR_TIMEOUT);
             }
           }
-          __nanosleep(128);  // the pieces still missing are being finished
         }
       }
       if (h == r) {
@@ -1669,28 +1653,22 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
     bool merged_here = npieces == 1;  // this CTA writes final records of the segment
     int mr = 0, mn = 1;                 // merger index and mergers of the segment
     if (npieces > 1) {
-      consumer_sync(kNCT);  // the piece's words are stored
-      if (deal.mode == 1) {
-        // round robin: the G CTAs of the group with the fewest tiles (the
-        // last indices) merge one q head each, waiting for the other pieces
-        // by their epochs - no counter; each CTA holds one piece, so a
-        // merger that waits holds up no other segment
-        mn = imin(G, npieces);
-        mr = npieces - 1 - ((int)blockIdx.x - c0);
-      } else {
-        // contiguous deal: the last to count merges alone; it never waits
-        // for a piece (an earlier merger would wait for CTAs still busy with
-        // earlier segments)
-        if (tid == 0) flags[1] = atomic_add_relaxed_gpu(&a.ws_counter[s], 1);
-        consumer_sync(kNCT);
-        mr = npieces - 1 - flags[1];  // 0: the last to count
-        if (mr == 0 && tid == 0) st_relaxed_gpu_s32(&a.ws_counter[s], 0);  // all have counted
-      }
+      consumer_sync(kNCT);
+      if (tid == 0) flags[1] = atomic_add_relaxed_gpu(&a.ws_counter[s], 1);
+      consumer_sync(kNCT);
+      // round robin: the last G to count merge (each CTA holds one piece, so
+      // a merger that waits for a later piece holds up no other segment);
+      // contiguous deal: only the last, which never waits for a piece (an
+      // earlier merger would wait for CTAs still busy with earlier segments)
+      mn = deal.mode == 1 ? imin(G, npieces) : 1;
+      mr = npieces - 1 - flags[1];  // 0: the last to count
       merged_here = mr < mn;
       if (tid == 0) stamp(kTrCounted);
       if (merged_here) {
         if (ring_free) merge_heads(b, g, s, c0, npieces, ep, mr, mn, smem, a.stages * a.stage_bytes);
         else merge_heads(b, g, s, c0, npieces, ep, mr, mn, reinterpret_cast<char*>(merge), kMergeBytes);
+        // every CTA has counted: the last one resets the counter
+        if (mr == 0 && tid == 0) st_relaxed_gpu_s32(&a.ws_counter[s], 0);
       }
     } else if (tid == 0) {
       stamp(kTrCounted);
