@@ -44,9 +44,9 @@ constexpr int kBM = 128;       // query rows per CTA
 constexpr int kBN = 128;       // keys per block
 constexpr float kRescaleLog2 = 8.0f;
 // Pairs of every 4 (per 8 keys) whose exponentials use the FMA-pipe
-// polynomial instead of MUFU.  Measured on B200: the softmax is issue-bound,
-// so moving work off MUFU costs more than it saves (0 of 4: 600 TFLOP/s,
-// 2 of 4: 549 TFLOP/s on config 5).
+// polynomial instead of MUFU.  Measured on B200 (config 5, before the
+// softmax ping-pong): 0 of 4 655 TFLOP/s, 1 of 4 678, 2 of 4 622, 3 of 4
+// 568 - the polynomial costs about as many issue slots as it frees on MUFU.
 constexpr int kPolyPairs = 0;
 
 struct PrefillArgs {
@@ -83,18 +83,25 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
+// The issuing helpers below are executed by a whole converged warp: the
+// operands are computed by every lane, so they stay warp-uniform (the tensor
+// core takes them from uniform registers), and `elect.sync` picks the one
+// lane that issues.
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
           smem_u32(bar))
       : "memory");
 }
 __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                            uint32_t idesc, uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred p, e;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
@@ -226,32 +233,87 @@ __device__ __forceinline__ uint32_t sw64_off(int rows, int cb, int row, int c) {
   return (uint32_t)(cb * rows * 64 + row * 64 + ((c ^ ((row >> 1) & 3)) << 4));
 }
 
+// Packed FP16 pairs into 32 TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+      "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+      "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+// D (TMEM) [+]= A (TMEM, FP16 pairs per 32-bit column) x B (shared memory);
+// issued like tc_mma_f16 by one elected lane of a converged warp.
+__device__ __forceinline__ void tc_mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Named barriers (ids 1 and 2) over the two softmax warpgroups (256 threads).
+__device__ __forceinline__ void named_sync(int id) {
+  asm volatile("bar.sync %0, 256;" ::"r"(id) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id) {
+  asm volatile("bar.arrive %0, 256;" ::"r"(id) : "memory");
+}
+
+// Register split of the warpgroups (setmaxnreg): the block launches with
+// kLaunchRegs a thread; the producer/MMA warpgroup gives back to kLowRegs,
+// the two softmax warpgroups take kHighRegs (2 * 128 * kHighRegs + 128 *
+// kLowRegs <= 384 * kLaunchRegs, the registers the block was launched with).
+// 72/208 is the split at which neither side spills for any head size (at
+// 40 registers the MMA issue loop spilled to local memory).
+constexpr int kLaunchRegs = 168, kLowRegs = 72, kHighRegs = 208;
+static_assert(2 * 128 * kHighRegs + 128 * kLowRegs <= 384 * kLaunchRegs, "register split");
+__device__ __forceinline__ void regs_low() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kLowRegs));
+}
+__device__ __forceinline__ void regs_high() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kHighRegs));
+}
+
 template <int HD, int NT>
 struct PrefillSmem {
+  static_assert(NT == 2, "two query tiles per CTA: two softmax warpgroups");
   static constexpr int kCB = HD / 32;                  // 32-half column blocks
   static constexpr int kQBytes = kBM * HD * 2;         // one Q tile
   static constexpr int kKVBytes = kBN * HD * 2;        // one K or V block
-  static constexpr int kPBytes = kBM * kBN * 2;        // P block, FP16
-  static constexpr int kKS = 2;                        // K ring depth
-  static constexpr int kVS = 2;                        // V ring depth
+  // ring depths: as deep as 227 KB allow (HD 96: 48 + 4 * 24 + 3 * 24 KB)
+  static constexpr int kKS = HD <= 96 ? 4 : 2;         // K ring depth
+  static constexpr int kVS = HD <= 64 ? 4 : HD <= 96 ? 3 : 2;  // V ring depth
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + NT * kQBytes;
   static constexpr int kOffV = kOffK + kKS * kKVBytes;
-  static constexpr int kOffP = kOffV + kVS * kKVBytes;
-  static constexpr int kOffBar = kOffP + NT * kPBytes;
+  static constexpr int kOffBar = kOffV + kVS * kKVBytes;
   // barriers: q_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
-  // per tile s_full, s_empty, p_full, pdone; mma_done
-  static constexpr int kNumBars = 1 + 2 * kKS + 2 * kVS + 4 * NT + 1;
+  // per tile s_full and p_full; mma_done
+  static constexpr int kNumBars = 1 + 2 * kKS + 2 * kVS + 2 * NT + 1;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 32;
-  static constexpr int kThreads = (4 * NT + 2) * 32;  // softmax warpgroups + producer + MMA
+  static constexpr int kThreads = (NT + 1) * 128;  // softmax warpgroups + producer/MMA warpgroup
 };
 
-// NT query tiles of 128 rows per CTA share every K/V block; tile t has its own
-// softmax warpgroup (warps 4t..4t+3), its own S (128 TMEM columns) and O
-// accumulator (next 128 columns).  The MMA thread alternates between tiles:
-// P_t(j) V_j, then S_t(j+1) = Q_t K_{j+1}^T, so one tile's MMAs run while the
-// other tile's softmax works.
+// NT = 2 query tiles of 128 rows per CTA share every K/V block.  Tile t owns
+// TMEM columns [256t, 256t + 256): S (128 columns; P, as FP16 pairs, is
+// written over its first 64 once the scores are read) and O (next HD
+// columns).  Per 128-key block j of tile t the MMA warp issues, once the
+// softmax has written P_t(j): O_t += P_t(j) V_j (A from TMEM), then
+// S_t(j+1) = Q_t K_{j+1}^T over the same columns (the tensor core runs them
+// in order, so P is read before it is overwritten), and one commit that
+// hands S_t(j+1) - and the finished P V - to the softmax.  While one tile's
+// softmax works, the tensor core runs the other tile's products.
+// Warps: 0-3 softmax of tile 0, 4-7 of tile 1, 8 Q and K loads, 9 MMA
+// issue, 10 V loads, 11 idle (setmaxnreg works on whole warpgroups).
 template <int HD, int NT>
 __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
     prefill_kernel(const __grid_constant__ PrefillArgs a) {
@@ -277,10 +339,8 @@ __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
   uint64_t* v_full = k_empty + KS;
   uint64_t* v_empty = v_full + VS;
   uint64_t* s_full = v_empty + VS;
-  uint64_t* s_empty = s_full + NT;
-  uint64_t* p_full = s_empty + NT;
-  uint64_t* pdone = p_full + NT;
-  uint64_t* mma_done = pdone + NT;
+  uint64_t* p_full = s_full + NT;
+  uint64_t* mma_done = p_full + NT;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SM::kOffMisc + 8);
 
@@ -296,9 +356,7 @@ __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
     }
     for (int t = 0; t < NT; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&s_empty[t], 4);
       mbar_init(&p_full[t], 4);
-      mbar_init(&pdone[t], 1);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -313,109 +371,109 @@ __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4 * NT) {
-    // ------------------------------------------------------------- producer
-    if (lane == 0) {
-      const uint64_t pol = l2_evict_first_policy();
-      mbar_arrive_expect_tx(q_full, NT * SM::kQBytes);
+  if (warp >= 4 * NT) {
+    regs_low();
+    if (warp == 4 * NT || warp == 4 * NT + 2) {
+      // ------------------------------------------------- producers: K and V
+      // one thread each, so that neither ring waits behind the other's
+      // free slot (K_j is freed once S(j) is done, V_j once P(j) V_j is)
+      if (lane == 0) {
+        const bool is_k = warp == 4 * NT;
+        const uint64_t pol = l2_evict_first_policy();
+        if (is_k) {
+          mbar_arrive_expect_tx(q_full, NT * SM::kQBytes);
 #pragma unroll
-      for (int t = 0; t < NT; ++t)
+          for (int t = 0; t < NT; ++t)
 #pragma unroll
-        for (int cb = 0; cb < SM::kCB; ++cb)
-          tma_load_2d(smem + SM::kOffQ + t * SM::kQBytes + cb * kBM * 64, &a.tq,
-                      h * HD + cb * 32, (qb * NT + t) * kBM, q_full, pol);
-      // K runs ahead of V: K_j is needed (and freed) one softmax step earlier
-      int jk = 0, jv = 0;
-      while (jk < nb_last || jv < nb_last) {
-        if (jk < nb_last && (jk <= jv + KS - 1 || jv >= nb_last)) {
-          const int st = jk % KS;
-          if (!mbar_wait(&k_empty[st], (uint32_t)(((jk / KS) & 1) ^ 1), abort_flag, a.status)) break;
-          char* sk = smem + SM::kOffK + st * SM::kKVBytes;
-          mbar_arrive_expect_tx(&k_full[st], SM::kKVBytes);
+            for (int cb = 0; cb < SM::kCB; ++cb)
+              tma_load_2d(smem + SM::kOffQ + t * SM::kQBytes + cb * kBM * 64, &a.tq,
+                          h * HD + cb * 32, (qb * NT + t) * kBM, q_full, pol);
+        }
+        const int S = is_k ? KS : VS;
+        uint64_t* full = is_k ? k_full : v_full;
+        uint64_t* empty = is_k ? k_empty : v_empty;
+        char* ring = smem + (is_k ? SM::kOffK : SM::kOffV);
+        const CUtensorMap* map = is_k ? &a.tk : &a.tv;
+        for (int j = 0; j < nb_last; ++j) {
+          const int st = j % S;
+          if (!mbar_wait(&empty[st], (uint32_t)(((j / S) & 1) ^ 1), abort_flag, a.status)) break;
+          char* dst = ring + st * SM::kKVBytes;
+          mbar_arrive_expect_tx(&full[st], SM::kKVBytes);
 #pragma unroll
           for (int cb = 0; cb < SM::kCB; ++cb)
-            tma_load_2d(sk + cb * kBN * 64, &a.tk, g * HD + cb * 32, jk * kBN, &k_full[st], pol);
-          ++jk;
-        } else {
-          const int st = jv % VS;
-          if (!mbar_wait(&v_empty[st], (uint32_t)(((jv / VS) & 1) ^ 1), abort_flag, a.status)) break;
-          char* sv = smem + SM::kOffV + st * SM::kKVBytes;
-          mbar_arrive_expect_tx(&v_full[st], SM::kKVBytes);
-#pragma unroll
-          for (int cb = 0; cb < SM::kCB; ++cb)
-            tma_load_2d(sv + cb * kBN * 64, &a.tv, g * HD + cb * 32, jv * kBN, &v_full[st], pol);
-          ++jv;
+            tma_load_2d(dst + cb * kBN * 64, map, g * HD + cb * 32, j * kBN, &full[st], pol);
         }
       }
-    }
-  } else if (warp == 4 * NT + 1) {
-    // ------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t kIdS = idesc_f16(kBM, kBN, false);
-      constexpr uint32_t kIdO = idesc_f16(kBM, HD, true);
-      bool ok = mbar_wait(q_full, 0, abort_flag, a.status);
-      auto issue_s = [&](int t, int j) {  // S_t(j) = Q_t K_j^T
-        const uint32_t sq = smem_u32(smem + SM::kOffQ + t * SM::kQBytes);
-        const uint32_t sk = smem_u32(smem + SM::kOffK + (j % KS) * SM::kKVBytes);
+    } else if (warp == 4 * NT + 1) {
+      // ----------------------------------------------------------- MMA issuer
+      // the whole warp runs the loop (uniform operands); one lane issues
+      {
+        constexpr uint32_t kIdS = idesc_f16(kBM, kBN, false);
+        constexpr uint32_t kIdO = idesc_f16(kBM, HD, true);
+        // every lane waits; the warp goes on together (all lanes agree on ok)
+        auto wwait = [&](uint64_t* bar, uint32_t parity) {
+          return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, a.status));
+        };
+        bool ok = wwait(q_full, 0);
+        auto issue_s = [&](int t, int j) {  // S_t(j) = Q_t K_j^T
+          const uint32_t sq = smem_u32(smem + SM::kOffQ + t * SM::kQBytes);
+          const uint32_t sk = smem_u32(smem + SM::kOffK + (j % KS) * SM::kKVBytes);
 #pragma unroll
-        for (int k = 0; k < HD / 16; ++k) {
-          const uint32_t off = (k >> 1) * kBM * 64 + (k & 1) * 32;
-          const uint64_t ad = smem_desc_sw64(sq + off, 16, 512);
-          const uint64_t bd = smem_desc_sw64(sk + (k >> 1) * kBN * 64 + (k & 1) * 32, 16, 512);
-          tc_mma_f16(tmem + 256 * t, ad, bd, kIdS, k > 0 ? 1u : 0u);
-        }
-        tc_commit(&s_full[t]);
-      };
-      auto issue_pv = [&](int t, int j) {  // O_t += P_t(j) V_j
-        const uint32_t sp = smem_u32(smem + SM::kOffP + t * SM::kPBytes);
-        const uint32_t sv = smem_u32(smem + SM::kOffV + (j % VS) * SM::kKVBytes);
-#pragma unroll
-        for (int k = 0; k < kBN / 16; ++k) {
-          // A = P (K-major over keys): column block k/2, 32-byte half k%2
-          const uint64_t ad = smem_desc_sw64(sp + (k >> 1) * kBM * 64 + (k & 1) * 32, 16, 512);
-          // B = V (MN-major: hd contiguous): 16 keys = two 8-row atoms of 512 B;
-          // LBO = stride between 32-half column blocks of hd
-          const uint64_t bd = smem_desc_sw64(sv + k * 1024, kBN * 64, 512);
-          tc_mma_f16(tmem + 256 * t + 128, ad, bd, kIdO, (j > 0 || k > 0) ? 1u : 0u);
-        }
-        tc_commit(&pdone[t]);
-      };
-      ok = ok && mbar_wait(&k_full[0], 0, abort_flag, a.status);
-      tc_fence_after();
-      for (int t = 0; t < NT; ++t) issue_s(t, 0);
-      tc_commit(&k_empty[0]);
-      for (int j = 0; j < nb_last; ++j) {
-        ok = ok && mbar_wait(&v_full[j % VS], (uint32_t)((j / VS) & 1), abort_flag, a.status);
-        const bool next_k = j + 1 < nb_last;
-        if (next_k)
-          ok = ok && mbar_wait(&k_full[(j + 1) % KS], (uint32_t)(((j + 1) / KS) & 1), abort_flag,
-                               a.status);
-        for (int t = 0; t < NT; ++t) {
-          const int nb_t = tile_blocks(qb * NT + t);
-          if (j >= nb_t) continue;
-          // S_t(j+1) first: the tile's next softmax waits on it, while
-          // P_t(j) V_j is needed only before P_t(j+1) is written
-          if (j + 1 < nb_t) {
-            ok = ok && mbar_wait(&s_empty[t], (uint32_t)(j & 1), abort_flag, a.status);
-            tc_fence_after();
-            issue_s(t, j + 1);
+          for (int k = 0; k < HD / 16; ++k) {
+            const uint32_t off = (k >> 1) * kBM * 64 + (k & 1) * 32;
+            const uint64_t ad = smem_desc_sw64(sq + off, 16, 512);
+            const uint64_t bd = smem_desc_sw64(sk + (k >> 1) * kBN * 64 + (k & 1) * 32, 16, 512);
+            tc_mma_f16(tmem + 256 * t, ad, bd, kIdS, k > 0 ? 1u : 0u);
           }
-          ok = ok && mbar_wait(&p_full[t], (uint32_t)(j & 1), abort_flag, a.status);
-          tc_fence_after();
-          issue_pv(t, j);
+        };
+        auto issue_pv = [&](int t, int j) {  // O_t += P_t(j) V_j, P from TMEM
+          const uint32_t sv = smem_u32(smem + SM::kOffV + (j % VS) * SM::kKVBytes);
+#pragma unroll
+          for (int k = 0; k < kBN / 16; ++k) {
+            // A = P: 16 keys = 8 columns of FP16 pairs; B = V (MN-major: hd
+            // contiguous): 16 keys = two 8-row atoms of 512 B, LBO = stride
+            // between 32-half column blocks of hd
+            const uint64_t bd = smem_desc_sw64(sv + k * 1024, kBN * 64, 512);
+            tc_mma_f16_ta(tmem + 256 * t + 128, tmem + 256 * t + 8 * k, bd, kIdO,
+                          (j > 0 || k > 0) ? 1u : 0u);
+          }
+        };
+        ok = ok && wwait(&k_full[0], 0);
+        tc_fence_after();
+        for (int t = 0; t < NT; ++t) {
+          issue_s(t, 0);
+          tc_commit(&s_full[t]);
         }
-        tc_commit(&v_empty[j % VS]);
-        if (next_k) tc_commit(&k_empty[(j + 1) % KS]);
+        tc_commit(&k_empty[0]);
+        for (int j = 0; j < nb_last; ++j) {
+          ok = ok && wwait(&v_full[j % VS], (uint32_t)((j / VS) & 1));
+          const bool next_k = j + 1 < nb_last;
+          if (next_k)
+            ok = ok && wwait(&k_full[(j + 1) % KS], (uint32_t)(((j + 1) / KS) & 1));
+          for (int t = 0; t < NT; ++t) {
+            const int nb_t = tile_blocks(qb * NT + t);
+            if (j >= nb_t) continue;
+            ok = ok && wwait(&p_full[t], (uint32_t)(j & 1));
+            tc_fence_after();
+            issue_pv(t, j);
+            if (j + 1 < nb_t) issue_s(t, j + 1);
+            tc_commit(&s_full[t]);  // S_t(j+1) (or, last block, the final P V) done
+          }
+          tc_commit(&v_empty[j % VS]);
+          if (next_k) tc_commit(&k_empty[(j + 1) % KS]);
+        }
+        // every MMA of this CTA has finished before TMEM is released (also on
+        // the drain path after a timed-out wait)
+        tc_commit(mma_done);
+        volatile int no_abort = 0;
+        mbar_wait(mma_done, 0, &no_abort, a.status);
+        __syncwarp();
+        (void)ok;
       }
-      // every MMA of this CTA has finished before TMEM is released (also on
-      // the drain path after a timed-out wait)
-      tc_commit(mma_done);
-      volatile int no_abort = 0;
-      mbar_wait(mma_done, 0, &no_abort, a.status);
-      (void)ok;
     }
-  } else if (warp < 4 * NT) {
+  } else {
     // ------------------------------------------------------------- softmax
+    regs_high();
     const int t = warp >> 2;                  // query tile of this warpgroup
     const int r = tid & 127;                  // row inside the tile (== TMEM lane)
     const int qt = qb * NT + t;               // global 128-row block of the tile
@@ -425,46 +483,40 @@ __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
     const uint32_t lane_sel = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + 256 * t + lane_sel;
     const uint32_t tO = tS + 128;
-    const int wg_bar = 2 + t;                 // named barrier of this warpgroup
-    (void)wg_bar;
     float m_ref = -INFINITY, l = 0.f;
     const float sl2 = a.scale_log2;
-    char* pb = smem + SM::kOffP + t * SM::kPBytes;
+    // The exp2 unit bounds the exponentials, so the two tiles take turns
+    // (ping-pong): in every block tile 0 runs its exponentials, then tile 1.
+    // Each tile loads its scores and takes the row max while the other one
+    // holds the turn.  Tile 0 waits (barrier 1) for tile 1's block j-1, tile
+    // 1 (barrier 2) for tile 0's block j, while the other tile has that block.
+    const int nb_o = tile_blocks(qb * NT + (NT - 1 - t));  // the other tile's blocks
     for (int j = 0; j < nb; ++j) {
       mbar_wait(&s_full[t], (uint32_t)(j & 1), abort_flag, a.status);
       tc_fence_after();
-      // pass 1: row max of the raw scores, two 64-column halves (4 chains);
-      // the causal mask only touches blocks holding a key past the tile's
-      // first position (the diagonal block, two when q_off % 128 != 0)
-      const bool diag = j * kBN + kBN - 1 > a.q_off + qt * kBM;
+      // the whole row of scores in one load; the causal mask touches only
+      // blocks holding a key past the tile's first position
+      float s[128];
+      tmem_ld128(tS, s);
+      if (j * kBN + kBN - 1 > a.q_off + qt * kBM) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (j * kBN + c > qpos) s[c] = -INFINITY;
+      }
       float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        float s[64];
-        tmem_ld64(tS + hh * 64, s);
-        if (diag) {
-#pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (j * kBN + hh * 64 + c > qpos) s[c] = -INFINITY;
-        }
-#pragma unroll
-        for (int c = 0; c < 64; c += 8) {
-          m4[0] = max3(m4[0], s[c], s[c + 1]);
-          m4[1] = max3(m4[1], s[c + 2], s[c + 3]);
-          m4[2] = max3(m4[2], s[c + 4], s[c + 5]);
-          m4[3] = max3(m4[3], s[c + 6], s[c + 7]);
-        }
+      for (int c = 0; c < 128; c += 8) {
+        m4[0] = max3(m4[0], s[c], s[c + 1]);
+        m4[1] = max3(m4[1], s[c + 2], s[c + 3]);
+        m4[2] = max3(m4[2], s[c + 4], s[c + 5]);
+        m4[3] = max3(m4[3], s[c + 6], s[c + 7]);
       }
       const float mx = max3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * sl2;
-      // P_t(j-1) and O_t: wait until P_t(j-1) V_{j-1} has finished
-      if (j > 0) {
-        mbar_wait(&pdone[t], (uint32_t)((j - 1) & 1), abort_flag, a.status);
-        tc_fence_after();
-      }
       if (j == 0) {
         m_ref = mx;
       } else if (__any_sync(0xffffffffu, mx > m_ref + kRescaleLog2)) {
-        // O holds sum_t 2^(s_t - m_ref) v_t: rescale it to the new max
+        // O holds sum_t 2^(s_t - m_ref) v_t (the P V of block j-1 finished
+        // before S(j) was handed over): rescale it to the new max
         const float mnew = fmaxf(m_ref, mx);
         const float alpha = ex2_ftz(m_ref - mnew);
         l *= alpha;
@@ -477,58 +529,56 @@ __global__ void __launch_bounds__(PrefillSmem<HD, NT>::kThreads, 1)
           for (int i = 0; i < 32; ++i) tt[i] *= alpha;
           tmem_st32(tO + c * 32, tt);
         }
-        tmem_wait_st();
       }
-      // pass 2: p = 2^(s - m_ref) <= 2^8, FP16 into the swizzled P buffer;
-      // per 8 keys kPolyPairs pairs use the FMA-pipe polynomial, the rest MUFU
+      if (t == 0) {
+        if (j >= 1 && j - 1 < nb_o) named_sync(1);
+      } else if (j < nb_o) {
+        named_sync(2);
+      }
+      // p = 2^(s - m_ref) <= 2^8, FP16 pairs over the first 64 S columns
       uint64_t rsum = pk2(0.f, 0.f);
       const uint64_t SL = pk2(sl2, sl2), NM = pk2(-m_ref, -m_ref);
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        float s[64];
-        tmem_ld64(tS + hh * 64, s);
-        if (diag) {
+        uint32_t w[32];
 #pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (j * kBN + hh * 64 + c > qpos) s[c] = -INFINITY;
-        }
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {  // 16-byte chunks of 8 keys
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const uint64_t X = fma2(pk2(s[ch * 8 + 2 * e], s[ch * 8 + 2 * e + 1]), SL, NM);
-            float x0, x1, p0, p1;
-            upk2(X, x0, x1);
-            if (e < kPolyPairs) {
-              exp2_poly_pair(x0, x1, p0, p1);
-            } else {
-              p0 = ex2_ftz(x0);
-              p1 = ex2_ftz(x1);
-            }
-            rsum = add2(rsum, pk2(p0, p1));
-            const __half2 hp = __floats2half2_rn(p0, p1);
-            w[e] = *reinterpret_cast<const uint32_t*>(&hp);
+        for (int e = 0; e < 32; ++e) {
+          const int c = hh * 64 + 2 * e;
+          const uint64_t X = fma2(pk2(s[c], s[c + 1]), SL, NM);
+          float x0, x1;
+          upk2(X, x0, x1);
+          // the exp2 unit alone would bound this loop: kPolyPairs of every
+          // 4 pairs use the FMA-pipe polynomial instead
+          float p0, p1;
+          if ((e & 3) < kPolyPairs) {
+            exp2_poly_pair(x0, x1, p0, p1);
+          } else {
+            p0 = ex2_ftz(x0);
+            p1 = ex2_ftz(x1);
           }
-          const int cg = hh * 8 + ch;  // chunk of the 128-key row
-          const uint32_t off = sw64_off(kBM, cg >> 2, r, cg & 3);
-          *reinterpret_cast<uint4*>(pb + off) = make_uint4(w[0], w[1], w[2], w[3]);
+          rsum = add2(rsum, pk2(p0, p1));
+          const __half2 hp = __floats2half2_rn(p0, p1);
+          w[e] = *reinterpret_cast<const uint32_t*>(&hp);
         }
+        tmem_st32u(tS + hh * 32, w);
       }
+      // hand the turn over
+      if (t == 0) {
+        if (j < nb_o) named_arrive(2);
+      } else if (j + 1 < nb_o) {
+        named_arrive(1);
+      }
+      tmem_wait_st();
       float rs0, rs1;
       upk2(rsum, rs0, rs1);
-      // S_t(j) has been read: the MMA may overwrite it with S_t(j+1)
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[t]);
       l += rs0 + rs1;
-      fence_proxy_async_smem();
+      // P_t(j) (and any O rescale) is in TMEM: the MMA may read it
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
     }
-    // epilogue: O / l
-    mbar_wait(&pdone[t], (uint32_t)((nb - 1) & 1), abort_flag, a.status);
+    // epilogue: O / l once the last P V has finished
+    mbar_wait(&s_full[t], (uint32_t)(nb & 1), abort_flag, a.status);
     tc_fence_after();
     const float inv = 1.f / l;
     float* orow = a.out + (int64_t)qi * a.n_heads * HD + (int64_t)h * HD;
@@ -615,10 +665,10 @@ int launch_prefill_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
     *err = "prefill head_dim must be 64, 96 or 128";
     return GLA_ERR_NOT_SUPPORTED;
   }
-  // two 128-row query tiles per CTA where shared memory allows, one otherwise
+  // two 128-row query tiles per CTA
   const size_t need = (head_dim == 64    ? PrefillSmem<64, 2>::kBytes
                        : head_dim == 96 ? PrefillSmem<96, 2>::kBytes
-                                        : PrefillSmem<128, 1>::kBytes) +
+                                        : PrefillSmem<128, 2>::kBytes) +
                       1024;
   if (need > (size_t)dev.smem_optin) {
     *err = "prefill shared memory layout does not fit";
@@ -648,7 +698,7 @@ int launch_prefill_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
   switch (head_dim) {
     case 64: return launch_hd<64, 2>(a, stream, err);
     case 96: return launch_hd<96, 2>(a, stream, err);
-    default: return launch_hd<128, 1>(a, stream, err);
+    default: return launch_hd<128, 2>(a, stream, err);
   }
 }
 
