@@ -29,8 +29,11 @@
 //    and no CTA-wide barrier is needed per tile.
 //  * At the end of a segment piece the warps merge their states in shared
 //    memory.  A segment held by one CTA is written straight to xb; otherwise
-//    each CTA stores its piece to a workspace slot and the last CTA to finish
-//    (atomic counter, reset by that CTA) merges the pieces (log-sum-exp).
+//    each CTA stores its piece to a workspace slot as 64-bit words tagged
+//    with the call's epoch and counts itself on the segment's counter; the
+//    last min(G, pieces) CTAs to count (round-robin deal; only the last in
+//    the contiguous deal) merge one q head each (log-sum-exp), and the last
+//    one resets the counter.
 //    Sharded sequences (record mode 2) then exchange per-rank records over
 //    peer memory and merge them in the same kernel (publish_merge).
 //
