@@ -418,6 +418,8 @@ def run_decode(args, key, rank, world, local_rank, dist, cpu_budget=8.0):
     esize = 2 if wl["f16"] else 4
     stream = torch.cuda.Stream(device)
     ctx = gla.Context(local_rank, stream.cuda_stream)
+    if args.trace:  # before any launch is captured: the stamps are launch arguments
+        ctx.set_option(gla.OPT_TRACE, 1)
     sharded = key == "c4" and world > 1
 
     # ---- per-rank work -----------------------------------------------------
@@ -547,6 +549,14 @@ def run_decode(args, key, rank, world, local_rank, dist, cpu_budget=8.0):
     st = ctx.device_status()
     if st != 0:
         raise RuntimeError(f"device status {st} after the timed region")
+    trace = None
+    if args.trace:  # phase timeline of the last timed launch, every rank
+        from gpullama_attn import phase_trace
+        mine = phase_trace.summarize_ctx(ctx, f"rank {rank}")
+        trace = [mine]
+        if dist is not None:
+            trace = [None] * world
+            dist.all_gather_object(trace, mine)
 
     # ---- e2e through the reference-facing calls with host buffers -----------
     e2e = None
@@ -624,6 +634,8 @@ def run_decode(args, key, rank, world, local_rank, dist, cpu_budget=8.0):
             else "nccl-allgather + combine kernel"
     if parity is not None:
         result["parity"] = parity
+    if trace is not None:
+        result["trace"] = trace
     if e2e is not None:
         result["e2e"] = e2e
     if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.quick):
@@ -632,13 +644,27 @@ def run_decode(args, key, rank, world, local_rank, dist, cpu_budget=8.0):
     return result
 
 
-def timed_loop(args, fn, torch, device, stream, dist):
-    """Warm-up, then device time per call (ms, CUDA events on the stream),
-    bounded below by the host wall time, max over ranks."""
+def timed_loop(args, fn, torch, device, stream, dist, soak_s=1.0):
+    """Warm-up, a soak of about soak_s seconds of the same calls (so the
+    timed steps run at the clocks of a sustained load, like the device-side
+    number measured after its own soak), then device time per call (ms, CUDA
+    events on the stream), bounded below by the host wall time, max over
+    ranks."""
     with torch.cuda.stream(stream):
         for _ in range(max(3, args.warmup)):
             fn()
     torch.cuda.synchronize(device)
+    if not args.quick and soak_s > 0:
+        per_iter = max(ms_est(fn, stream, torch, device), 1e-3)
+        n = int(min(5000, max(1, soak_s * 1000.0 / per_iter)))
+        if dist is not None:  # every rank issues the same calls
+            t = torch.tensor([n], device=device, dtype=torch.int64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            n = int(t.item())
+        with torch.cuda.stream(stream):
+            for _ in range(n):
+                fn()
+        torch.cuda.synchronize(device)
     if dist is not None:
         dist.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
@@ -1276,6 +1302,10 @@ def main():
     ap.add_argument("--quick", action="store_true",
                     help="profiling runs: no clock soak, no e2e loop, no CPU baseline, no "
                          "parity check, no extras")
+    ap.add_argument("--trace", action="store_true",
+                    help="decode workloads: add every rank's per-CTA phase timeline of the "
+                         "last timed launch (stamps in every launch: a diagnostic run, not "
+                         "the headline number)")
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling runs: fewer layers than the workload's (same per-layer "
                          "launch), to keep an ncu capture small")
