@@ -1615,18 +1615,12 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
 
   // ring_free: no tiles of a later piece of this CTA are in flight or staged.
   auto finish_piece = [&](int b, int g, bool ring_free, bool first) {
-    const int s = b * n_kv + g;
-    int32_t c0;
-    const int32_t npieces = deal.pieces(seq_start, nunits, b, g, &c0);
-    // count this piece before folding and storing it: the atomic's round trip
-    // overlaps that work (its value is read only after the stores).  A merger
-    // may therefore see a piece counted before its words are stored; it
-    // recognises them by their epoch and copies them again.
-    int32_t ticket = 0;
-    if (npieces > 1 && tid == 0) ticket = atomic_add_relaxed_gpu(&a.ws_counter[s], 1);
     cons.to_merge(a, merge_w, lane);
     if (first && tid == 0) mbar_wait(ep_bar, 0, flags, a.status);  // flags[4]: the call epoch
     consumer_sync(kNCT);
+    const int s = b * n_kv + g;
+    int32_t c0;
+    const int32_t npieces = deal.pieces(seq_start, nunits, b, g, &c0);
     const uint32_t ep = (uint32_t)flags[4];
     // one thread per (head, 4 columns): the warps' (m, l) pairs, then their
     // o chunks, as float2 / float4 shared loads
@@ -1662,7 +1656,8 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
     bool merged_here = npieces == 1;  // this CTA writes final records of the segment
     int mr = 0, mn = 1;                 // merger index and mergers of the segment
     if (npieces > 1) {
-      if (tid == 0) flags[1] = ticket;
+      consumer_sync(kNCT);
+      if (tid == 0) flags[1] = atomic_add_relaxed_gpu(&a.ws_counter[s], 1);
       consumer_sync(kNCT);
       // round robin: the last G to count merge (each CTA holds one piece, so
       // a merger that waits for a later piece holds up no other segment);
