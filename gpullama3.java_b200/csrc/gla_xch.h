@@ -14,7 +14,9 @@
 //
 //   records  [2][kXchMaxWorld][kXchRecWords]   uint64
 //   epochs   [kXchMaxSeg] uint32: calls completed for kv head g on this rank,
-//            read and advanced only by the CTA that publishes g (one per call)
+//            read by every CTA holding a piece of g and advanced once a call
+//            by g's merger 0 (the last of g's mergers to count; each merger
+//            publishes its own q heads of g)
 #pragma once
 
 #include <stddef.h>
