@@ -912,8 +912,12 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
   volatile int* flags = reinterpret_cast<volatile int*>(smem + a.off_flags);
   float2* rope_cs = reinterpret_cast<float2*>(smem + a.off_rope);      // [HD/2] (fused RoPE)
   // phase stamps (a.trace lives in the parameter bank: no register stays live)
+  // Only the tensor-map loader's launches are traced: in the two-CTA
+  // batched kernel (cp.async loader, 168 registers) the trace code alone made
+  // the compiler spill.
+  constexpr bool kTraced = LOADER == 0;
   auto stamp = [&](int slot) {
-    if (a.trace) a.trace[(size_t)blockIdx.x * kTraceWords + slot] = global_timer_ns();
+    if (kTraced && a.trace) a.trace[(size_t)blockIdx.x * kTraceWords + slot] = global_timer_ns();
   };
 
   // The deal's mode does not depend on the lengths (see make_deal).  The
@@ -1586,7 +1590,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
       }
       if (h == r) {
         ck[4] = clock64();
-        if (a.trace && tid == 0) {
+        if (kTraced && a.trace && tid == 0) {
           auto d16 = [](long long x) { return (uint64_t)(x > 65535 ? 65535 : x); };
           a.trace[(size_t)blockIdx.x * kTraceWords + kTrMergeCycles] =
               d16(ck[1] - ck[0]) | (d16(ck[2] - ck[1]) << 16) | (d16(ck[3] - ck[2]) << 32) |
@@ -1702,7 +1706,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
     for (; row0 < row_end; row0 += row_step) {
       const int rows = imin(unit_rows, np - row0);
       mbar_wait(&full[st], phase, flags, a.status);
-      if (a.trace && tid == 0 && flags[6] == 0) {
+      if (kTraced && a.trace && tid == 0 && flags[6] == 0) {
         stamp(kTrFirstTile);
         flags[6] = 1;
       }
@@ -1734,7 +1738,7 @@ __global__ void __launch_bounds__((Consumer::kNW + 1) * 32,
       first = false;
     }
   }
-  if (a.trace && tid == 0) {
+  if (kTraced && a.trace && tid == 0) {
     uint32_t smid;
     asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
     a.trace[(size_t)blockIdx.x * kTraceWords + kTrInfo] =
