@@ -129,7 +129,8 @@ int32_t gla_num_sms(const gla_ctx* ctx);
  * GLA_ERR_TIMEOUT and sharded decode needs gla_comm_init again.  No
  * reference counterpart (the reference is single-device). */
 #define GLA_OPT_TRACE 4
-/* GLA_OPT_TRACE (default 0): 1 = every decode call on the context writes
+/* GLA_OPT_TRACE (default 0): 1 = every single-sequence or sharded decode
+ * call on the context (batched calls leave none) writes
  * %globaltimer stamps of its phases (16 words per CTA: entry, dependency
  * wait, q loaded, first tile, last tile, piece counted, merged, published,
  * producer first/last copy, info, exit), read back with gla_debug_trace.
